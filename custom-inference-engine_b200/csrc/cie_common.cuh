@@ -1,0 +1,59 @@
+// cie_common.cuh — shared host/device definitions of libcie_attn.so:
+// the per-device status word, the thread-local error message and argument
+// checking helpers used by every C-ABI entry point.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+
+#include "../../include/cie_attn.h"
+
+namespace cie {
+
+// Per-device status word. Kernels OR CIE_DEV_* bits into it when they detect
+// a bad block id, an out-of-table RoPE position or a wait that timed out;
+// cie_device_status() reads and optionally clears it. The library is built as
+// one translation unit (libcie_attn.cu), so this is its only definition.
+__device__ unsigned int g_device_status = 0;
+
+__device__ __forceinline__ void raise_status(unsigned int bits) {
+  atomicOr(&g_device_status, bits);
+}
+
+// Upper bound for any single pipeline wait inside a kernel (nanoseconds).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// ---------------------------------------------------------------- host side
+void set_error(const char* fmt, ...);
+
+#define CIE_CHECK_ARG(cond, ...)        \
+  do {                                  \
+    if (!(cond)) {                      \
+      ::cie::set_error(__VA_ARGS__);    \
+      return CIE_ERR_INVALID;           \
+    }                                   \
+  } while (0)
+
+#define CIE_CHECK_LAUNCH(what)                                                        \
+  do {                                                                                \
+    cudaError_t e__ = cudaGetLastError();                                             \
+    if (e__ != cudaSuccess) {                                                         \
+      ::cie::set_error("%s: launch failed: %s", what, cudaGetErrorString(e__));       \
+      return CIE_ERR_LAUNCH;                                                          \
+    }                                                                                 \
+  } while (0)
+
+inline int num_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) {
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n > 0 ? n : 148;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace cie

@@ -1,0 +1,623 @@
+// prefill_attn.cu — causal / non-causal grouped-query flash attention for
+// prefill on sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// Semantics follow kernels/ref/flash_attention_ref.py:8-56 (fp32 reference)
+// and the Triton entry kernels/flash_attention.py:136-209: out = softmax(
+// q k^T * scale + bottom-right causal mask) v, with the kv head of q head h
+// being h / (Hq / Hkv) (no K/V expansion), optional half-split RoPE of q
+// applied to the Q tile in shared memory (kernels/ref/rope_apply_ref.py:22-53).
+//
+// One CTA owns a 128-row query tile of one (batch, head) and streams 128-key
+// K/V tiles:
+//   warp 0      TMA producer: Q once, then K_j / V_j into a ring of stages
+//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer:
+//                 S_j = Q K_j^T   (SS MMA, fp32 in TMEM, double-buffered)
+//                 O  += P_j V_j   (TS MMA, P read from TMEM, V MN-major)
+//   warps 2..5  softmax: thread r owns query row r == TMEM lane r, so row
+//               max / sum need no cross-thread reduction; writes P (16-bit)
+//               back to TMEM; rescales O in TMEM only when the running max
+//               grew by more than 2^8 (the stale max is exact because O and
+//               the row sum share it); epilogue O / l -> global.
+// Causal tiles are ordered heaviest first across the grid.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <type_traits>
+
+#include "cie_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace cie {
+
+constexpr int kPfThreads = 192;
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+
+template <int D>
+struct PfCfg {
+  static constexpr int KCH = D / 64;                 // 128-byte swizzle chunks along d
+  static constexpr int Q_BYTES = kBM * D * 2;
+  static constexpr int KV_BYTES = kBN * D * 2;
+  static constexpr int STAGES = (D == 64) ? 4 : 2;
+  static constexpr int BAR_OFF = Q_BYTES + 2 * STAGES * KV_BYTES;
+  static constexpr int NBARS = 2 + 4 * STAGES + 2 + 2 + 2 + 1 + 1;
+  static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 /*tmem slot, abort*/ + 1024 /*align*/;
+  static constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_P0 = 256, TM_P1 = 320, TM_O = 384;
+  static constexpr uint32_t TM_COLS = 512;
+};
+
+struct PrefillParams {
+  int B, Hq, Hkv, M, N, G;
+  int n_qtiles;
+  float scale_log2;
+  int causal;
+  void* o;
+  int64_t o_sb, o_sh, o_sm;
+  const float* cos;
+  const float* sin;
+  int rope_max_pos;
+  int rope_q_pos0;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
+  using C = PfCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + C::Q_BYTES;
+  uint8_t* sV = sK + C::STAGES * C::KV_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* bar_q_full = bars + 0;
+  uint64_t* bar_q_ready = bars + 1;
+  uint64_t* bar_k_full = bars + 2;
+  uint64_t* bar_k_empty = bar_k_full + C::STAGES;
+  uint64_t* bar_v_full = bar_k_empty + C::STAGES;
+  uint64_t* bar_v_empty = bar_v_full + C::STAGES;
+  uint64_t* bar_s_full = bar_v_empty + C::STAGES;  // [2]
+  uint64_t* bar_s_free = bar_s_full + 2;           // [2]
+  uint64_t* bar_p_full = bar_s_free + 2;           // [2]
+  uint64_t* bar_o_done = bar_p_full + 2;           // [1]
+  uint64_t* bar_drain = bar_o_done + 1;            // [1] abort path only
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // heaviest query tiles first when causal
+  const int bh_count = p.B * p.Hq;
+  const int qt_lin = blockIdx.x / bh_count;
+  const int qt = p.causal ? (p.n_qtiles - 1 - qt_lin) : qt_lin;
+  const int bh = blockIdx.x % bh_count;
+  const int b = bh / p.Hq;
+  const int h = bh % p.Hq;
+  const int kvh = h / p.G;
+  const int m0 = qt * kBM;
+  int n_end = p.causal ? min(p.N, p.N - p.M + m0 + kBM) : p.N;
+  if (n_end < 0) n_end = 0;
+  const int n_kv = (n_end + kBN - 1) / kBN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q_full, 1);
+    mbar_init(bar_q_ready, 128);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar_k_full + s, 1);
+      mbar_init(bar_k_empty + s, 1);
+      mbar_init(bar_v_full + s, 1);
+      mbar_init(bar_v_empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_s_full + s, 1);
+      mbar_init(bar_s_free + s, 128);
+      mbar_init(bar_p_full + s, 128);
+    }
+    mbar_init(bar_o_done, 1);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0 && n_kv > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < C::KCH; ++c)
+        tma_load_4d(sQ + c * kBM * 128, &tm_q, bar_q_full, c * 64, m0, h, b);
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % C::STAGES;
+        const uint32_t ph = (j / C::STAGES) & 1;
+        if (!mbar_wait_bounded(bar_k_empty + st, ph ^ 1, abort_flag, kWaitLimitNs)) break;
+        mbar_arrive_expect_tx(bar_k_full + st, C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(sK + st * C::KV_BYTES + c * kBN * 128, &tm_k, bar_k_full + st, c * 64,
+                      j * kBN, kvh, b);
+        issued_k = j + 1;
+        if (!mbar_wait_bounded(bar_v_empty + st, ph ^ 1, abort_flag, kWaitLimitNs)) break;
+        mbar_arrive_expect_tx(bar_v_full + st, C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(sV + st * C::KV_BYTES + c * kBN * 128, &tm_v, bar_v_full + st, c * 64,
+                      j * kBN, kvh, b);
+        issued_v = j + 1;
+      }
+      if (*abort_flag) {
+        // let this CTA's copies still in flight land before its smem is released:
+        // the newest load of each stage is the latest phase of that stage's barrier
+        mbar_wait_timeout(bar_q_full, 0, kWaitLimitNs);
+        for (int j = issued_k - 1; j >= 0 && j >= issued_k - C::STAGES; --j)
+          mbar_wait_timeout(bar_k_full + (j % C::STAGES), (j / C::STAGES) & 1, kWaitLimitNs);
+        for (int j = issued_v - 1; j >= 0 && j >= issued_v - C::STAGES; --j)
+          mbar_wait_timeout(bar_v_full + (j % C::STAGES), (j / C::STAGES) & 1, kWaitLimitNs);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0 && n_kv > 0) {
+      constexpr int fmt = BF16 ? 1 : 0;
+      constexpr uint32_t idesc_s = umma_idesc_f16(kBM, kBN, fmt, 0, 0);
+      constexpr uint32_t idesc_o = umma_idesc_f16(kBM, D, fmt, 0, 1);
+      const uint32_t q_base = smem_u32(sQ);
+      const uint32_t k_base = smem_u32(sK);
+      const uint32_t v_base = smem_u32(sV);
+      bool ok = mbar_wait_bounded(bar_q_ready, 0, abort_flag, kWaitLimitNs);
+      tc_fence_after();
+
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        const int s = i & 1;
+        const uint32_t sp = (i >> 1) & 1;
+        if (!mbar_wait_bounded(bar_p_full + s, sp, abort_flag, kWaitLimitNs)) return false;
+        if (!mbar_wait_bounded(bar_v_full + st, ph, abort_flag, kWaitLimitNs)) return false;
+        tc_fence_after();
+        const uint32_t p_col = s ? C::TM_P1 : C::TM_P0;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bdesc = umma_smem_desc(v_base + st * C::KV_BYTES + kk * 16 * 128,
+                                                kBN * 128, 1024);
+          umma_ts(tmem + C::TM_O, tmem + p_col + kk * 8, bdesc, idesc_o,
+                  (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar_o_done);
+        umma_commit(bar_v_empty + st);
+        return true;
+      };
+
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % C::STAGES;
+        const uint32_t ph = (j / C::STAGES) & 1;
+        const int s = j & 1;
+        const uint32_t sp = (j >> 1) & 1;
+        if (!mbar_wait_bounded(bar_k_full + st, ph, abort_flag, kWaitLimitNs)) { ok = false; break; }
+        if (!mbar_wait_bounded(bar_s_free + s, sp ^ 1, abort_flag, kWaitLimitNs)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t s_col = s ? C::TM_S1 : C::TM_S0;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int c = kk >> 2;
+          const uint32_t off = (kk & 3) * 32;
+          const uint64_t adesc = umma_smem_desc(q_base + c * kBM * 128 + off, 16, 1024);
+          const uint64_t bdesc =
+              umma_smem_desc(k_base + st * C::KV_BYTES + c * kBN * 128 + off, 16, 1024);
+          umma_ss(tmem + s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar_s_full + s);
+        umma_commit(bar_k_empty + st);
+        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok) ok = issue_pv(n_kv - 1);
+      if (!ok) {
+        raise_status(CIE_DEV_TIMEOUT);
+        umma_commit(bar_drain);  // all MMAs issued so far must finish before TMEM is freed
+        mbar_wait_timeout(bar_drain, 0, kWaitLimitNs);
+      }
+    }
+  } else {
+    // ------------------------------------------------ softmax warpgroup
+    const int wq = warp & 3;            // TMEM lane quarter this warp may access
+    const int row = wq * 32 + lane;     // query row within the tile == TMEM lane
+    const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
+    const int gm = m0 + row;            // global query index
+    using elem_t = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+
+    if (n_kv == 0) {
+      // no visible keys: N == 0 -> zeros (matches the fp32 reference), else NaN rows
+      if (gm < p.M) {
+        elem_t* o = reinterpret_cast<elem_t*>(p.o) + b * p.o_sb + h * p.o_sh + gm * p.o_sm;
+        const float fill = (p.N == 0) ? 0.f : __int_as_float(0x7fc00000);
+        for (int d = 0; d < D; ++d) {
+          if constexpr (BF16) o[d] = __float2bfloat16_rn(fill);
+          else o[d] = __float2half_rn(fill);
+        }
+      }
+    } else {
+      bool ok = mbar_wait_bounded(bar_q_full, 0, abort_flag, kWaitLimitNs);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok && p.cos != nullptr && gm < p.M) {
+        // rotate this thread's Q row in shared memory (half-split RoPE)
+        int pos = p.rope_q_pos0 + gm;
+        if (pos < 0 || pos >= p.rope_max_pos) {
+          raise_status(CIE_DEV_BAD_POSITION);
+          pos = pos < 0 ? 0 : p.rope_max_pos - 1;
+        }
+        constexpr int HALF = D / 2;
+        const float* cr = p.cos + static_cast<int64_t>(pos) * HALF;
+        const float* sr = p.sin + static_cast<int64_t>(pos) * HALF;
+#pragma unroll
+        for (int pc = 0; pc < HALF / 8; ++pc) {
+          const int e_lo = pc * 8, e_hi = HALF + pc * 8;
+          uint8_t* a_lo = sQ + (e_lo / 64) * kBM * 128 + row * 128 +
+                          ((((e_lo % 64) / 8) ^ (row & 7)) * 16);
+          uint8_t* a_hi = sQ + (e_hi / 64) * kBM * 128 + row * 128 +
+                          ((((e_hi % 64) / 8) ^ (row & 7)) * 16);
+          uint4 x1 = *reinterpret_cast<uint4*>(a_lo);
+          uint4 x2 = *reinterpret_cast<uint4*>(a_hi);
+          const uint32_t* u1 = reinterpret_cast<const uint32_t*>(&x1);
+          const uint32_t* u2 = reinterpret_cast<const uint32_t*>(&x2);
+          uint4 y1, y2;
+          uint32_t* w1 = reinterpret_cast<uint32_t*>(&y1);
+          uint32_t* w2 = reinterpret_cast<uint32_t*>(&y2);
+          const float4 ca = *reinterpret_cast<const float4*>(cr + e_lo);
+          const float4 cb = *reinterpret_cast<const float4*>(cr + e_lo + 4);
+          const float4 sa = *reinterpret_cast<const float4*>(sr + e_lo);
+          const float4 sb = *reinterpret_cast<const float4*>(sr + e_lo + 4);
+          const float cc[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+          const float ss[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f1 = unpack2<BF16>(u1[e]);
+            const float2 f2 = unpack2<BF16>(u2[e]);
+            const float c0 = cc[2 * e], c1 = cc[2 * e + 1];
+            const float s0 = ss[2 * e], s1 = ss[2 * e + 1];
+            w1[e] = pack2<BF16>(__fsub_rn(__fmul_rn(f1.x, c0), __fmul_rn(f2.x, s0)),
+                                __fsub_rn(__fmul_rn(f1.y, c1), __fmul_rn(f2.y, s1)));
+            w2[e] = pack2<BF16>(__fadd_rn(__fmul_rn(f1.x, s0), __fmul_rn(f2.x, c0)),
+                                __fadd_rn(__fmul_rn(f1.y, s1), __fmul_rn(f2.y, c1)));
+          }
+          *reinterpret_cast<uint4*>(a_lo) = y1;
+          *reinterpret_cast<uint4*>(a_hi) = y2;
+        }
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(bar_q_ready);
+
+      const int lim = p.causal ? (p.N - p.M + gm) : (p.N - 1);  // keys <= lim are visible
+      float m_run = -INFINITY;  // running max, log2 domain, scaled
+      float l_run = 0.f;
+      float sv[kBN];
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j & 1;
+        const uint32_t sp = (j >> 1) & 1;
+        ok = mbar_wait_bounded(bar_s_full + s, sp, abort_flag, kWaitLimitNs);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t s_col = s ? C::TM_S1 : C::TM_S0;
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c)
+          tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bar_s_free + s);
+
+        const int n0 = j * kBN;
+        if (n0 + kBN - 1 > lim) {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (n0 + c > lim) sv[c] = -INFINITY;
+        }
+        float mx = sv[0];
+#pragma unroll
+        for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
+        const float m_new = fmaxf(m_run, mx * p.scale_log2);
+
+        if (j > 0) {
+          ok = mbar_wait_bounded(bar_o_done, (j - 1) & 1, abort_flag, kWaitLimitNs);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          const bool need = m_new > m_run + 8.0f;
+          if (__any_sync(0xffffffffu, need)) {
+            const float alpha = need ? ex2(m_run - m_new) : 1.0f;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t ov[32];
+              tmem_ld32(tmem + lane_addr + C::TM_O + c * 32, ov);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+              tmem_st32(tmem + lane_addr + C::TM_O + c * 32, ov);
+            }
+            tmem_wait_st();
+            if (need) {
+              l_run *= alpha;
+              m_run = m_new;
+            }
+          }
+        } else {
+          m_run = m_new;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        const uint32_t p_col = s ? C::TM_P1 : C::TM_P0;
+        float lsum = 0.f;
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const float p0 = ex2(fmaf(sv[hb * 64 + c], p.scale_log2, -m_use));
+            const float p1 = ex2(fmaf(sv[hb * 64 + c + 1], p.scale_log2, -m_use));
+            lsum += p0 + p1;
+            pk[c / 2] = pack2<BF16>(p0, p1);
+          }
+          tmem_st32(tmem + lane_addr + p_col + hb * 32, pk);
+        }
+        l_run += lsum;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_p_full + s);
+      }
+
+      if (ok) {
+        ok = mbar_wait_bounded(bar_o_done, (n_kv - 1) & 1, abort_flag, kWaitLimitNs);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        const float inv_l = (l_run > 0.f) ? 1.0f / l_run : __int_as_float(0x7fc00000);
+        elem_t* o = reinterpret_cast<elem_t*>(p.o) + b * p.o_sb + h * p.o_sh + gm * p.o_sm;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(tmem + lane_addr + C::TM_O + c * 32, ov);
+          tmem_wait_ld();
+          if (gm < p.M) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              pk[e] = pack2<BF16>(__uint_as_float(ov[2 * e]) * inv_l,
+                                  __uint_as_float(ov[2 * e + 1]) * inv_l);
+            uint4* dst = reinterpret_cast<uint4*>(o + c * 32);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+          }
+        }
+      } else {
+        raise_status(CIE_DEV_TIMEOUT);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    tmem_dealloc(tmem, C::TM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                    CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(ptr);
+  });
+  return fn;
+}
+
+// 4-D map over (d, seq, head, batch) with a (64, 128, 1, 1) box, 128B swizzle.
+static int make_map(CUtensorMap* map, const void* base, int d, int seq, int heads, int batch,
+                    const int64_t* strides, bool bf16, const char* what) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) {
+    set_error("%s: cuTensorMapEncodeTiled unavailable", what);
+    return CIE_ERR_LAUNCH;
+  }
+  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)seq, (cuuint64_t)heads, (cuuint64_t)batch};
+  cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * 2, (cuuint64_t)strides[1] * 2,
+                        (cuuint64_t)strides[0] * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   4, const_cast<void*>(base), dims, gstr, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+    return CIE_ERR_INVALID;
+  }
+  return CIE_OK;
+}
+
+template <int D, bool BF16>
+static int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                          const PrefillParams& prm, cudaStream_t st) {
+  constexpr int smem = PfCfg<D>::SMEM;
+  auto kern = prefill_attn_kernel<D, BF16>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const int grid = prm.n_qtiles * prm.B * prm.Hq;
+  kern<<<grid, kPfThreads, smem, st>>>(mq, mk, mv, prm);
+  CIE_CHECK_LAUNCH("prefill_attn_kernel");
+  return CIE_OK;
+}
+
+int rope_launch(const void* x, void* y, int B, int H, int L, int d, const int64_t* xs,
+                const int64_t* ys, int pos0, bool bf16, const float* cos, const float* sin,
+                int max_pos, cudaStream_t st);
+size_t dense_mma_workspace(int B, int Hq, int Hkv, int M, int N, int d);
+int dense_mma_attn(const void* q, const void* k, const void* v, void* o, int B, int Hq, int Hkv,
+                   int M, int N, int d, const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                   const int64_t* os, float scale, int causal, bool bf16, const float* cos,
+                   const float* sin, int max_pos, int q_pos0, void* workspace,
+                   size_t workspace_bytes, cudaStream_t st);
+
+// The tcgen05 kernel takes head dims 64 / 128 with at least one full query
+// tile's worth of rows per kv head; short query blocks (decode-like, G*M <= 64)
+// and other head dims go to the split-KV mma.sync kernel over dense K/V.
+static bool use_tcgen05(int Hq, int Hkv, int M, int d) {
+  return (d == 64 || d == 128) && static_cast<int64_t>(Hq / Hkv) * M > 64;
+}
+
+static size_t rope_k_bytes(int B, int Hkv, int N, int d) {
+  return (static_cast<size_t>(B) * Hkv * N * d * 2 + 255) & ~size_t(255);
+}
+
+}  // namespace cie
+
+using namespace cie;
+
+extern "C" size_t cie_prefill_attn_workspace(int B, int Hq, int Hkv, int M, int N, int d,
+                                             int dtype, int rope_k) {
+  (void)dtype;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || M <= 0 || N < 0 || d <= 0) return 0;
+  size_t bytes = (rope_k && N > 0) ? rope_k_bytes(B, Hkv, N, d) : 0;
+  if (!use_tcgen05(Hq, Hkv, M, d)) bytes += dense_mma_workspace(B, Hq, Hkv, M, N, d);
+  return bytes > 0 ? bytes + 256 : 0;
+}
+
+extern "C" int cie_prefill_attn(const void* q, const void* k, const void* v, void* o, int B,
+                                int Hq, int Hkv, int M, int N, int d, const int64_t* q_strides,
+                                const int64_t* k_strides, const int64_t* v_strides,
+                                const int64_t* o_strides, float scale, int causal, int dtype,
+                                const float* rope_cos, const float* rope_sin, int rope_max_pos,
+                                int rope_q_pos0, int rope_k, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  CIE_CHECK_ARG(q && o && (N == 0 || (k && v)), "cie_prefill_attn: null tensor pointer");
+  CIE_CHECK_ARG(q_strides && k_strides && v_strides && o_strides,
+                "cie_prefill_attn: null strides");
+  CIE_CHECK_ARG(B >= 0 && Hq > 0 && Hkv > 0 && M >= 0 && N >= 0, "cie_prefill_attn: bad shape");
+  CIE_CHECK_ARG(Hq % Hkv == 0, "cie_prefill_attn: Hq (%d) must be a multiple of Hkv (%d)", Hq,
+                Hkv);
+  CIE_CHECK_ARG(dtype == CIE_DTYPE_BF16 || dtype == CIE_DTYPE_FP16,
+                "cie_prefill_attn: bad dtype %d", dtype);
+  CIE_CHECK_ARG((rope_cos == nullptr) == (rope_sin == nullptr),
+                "cie_prefill_attn: rope_cos and rope_sin must both be given or both NULL");
+  CIE_CHECK_ARG(rope_cos == nullptr || rope_max_pos > 0, "cie_prefill_attn: rope_max_pos <= 0");
+  CIE_CHECK_ARG(!(rope_k && rope_cos == nullptr), "cie_prefill_attn: rope_k needs rope tables");
+  if (d != 16 && d != 32 && d != 64 && d != 128 && d != 256) {
+    set_error("cie_prefill_attn: head_dim %d unsupported (16, 32, 64, 128 or 256)", d);
+    return CIE_ERR_UNSUPPORTED;
+  }
+  if (B == 0 || M == 0) return CIE_OK;
+  CIE_CHECK_ARG(rope_cos == nullptr || (aligned16(rope_cos) && aligned16(rope_sin)),
+                "cie_prefill_attn: rope tables must be 16-byte aligned");
+  const int64_t* all[4] = {q_strides, k_strides, v_strides, o_strides};
+  for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 3; ++j)
+      CIE_CHECK_ARG(all[i][j] % 8 == 0 && all[i][j] >= 0,
+                    "cie_prefill_attn: strides must be non-negative multiples of 8 elements");
+  CIE_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o),
+                "cie_prefill_attn: tensors must be 16-byte aligned");
+  const bool bf16 = dtype == CIE_DTYPE_BF16;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+  const void* kk = k;
+  int64_t kws[3];
+  const int64_t* ks = k_strides;
+  const size_t need = cie_prefill_attn_workspace(B, Hq, Hkv, M, N, d, dtype, rope_k);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) {
+    set_error("cie_prefill_attn: workspace of %zu bytes required, got %zu", need,
+              workspace_bytes);
+    return CIE_ERR_WORKSPACE;
+  }
+  uint8_t* ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(workspace) + 255) &
+                                           ~uintptr_t(255));
+  size_t ws_left = need > 256 ? need - 256 : 0;
+  if (rope_k && N > 0) {
+    void* kr = ws;
+    ws += rope_k_bytes(B, Hkv, N, d);
+    ws_left -= rope_k_bytes(B, Hkv, N, d);
+    kws[0] = static_cast<int64_t>(Hkv) * N * d;
+    kws[1] = static_cast<int64_t>(N) * d;
+    kws[2] = d;
+    int rc = rope_launch(k, kr, B, Hkv, N, d, k_strides, kws, 0, bf16, rope_cos, rope_sin,
+                         rope_max_pos, st);
+    if (rc != CIE_OK) return rc;
+    kk = kr;
+    ks = kws;
+  }
+
+  const int q_pos0_eff = rope_q_pos0;
+  if (N == 0) {
+    // no keys: the short-query kernel writes zeros and never reads K/V
+    kk = q;
+    v = q;
+    ks = q_strides;
+    v_strides = q_strides;
+  }
+  if (N == 0 || !use_tcgen05(Hq, Hkv, M, d))
+    return dense_mma_attn(q, kk, v, o, B, Hq, Hkv, M, N, d, q_strides, ks, v_strides, o_strides,
+                          scale, causal, bf16, rope_cos, rope_sin, rope_max_pos, q_pos0_eff, ws,
+                          ws_left, st);
+
+  PrefillParams prm{};
+  prm.B = B;
+  prm.Hq = Hq;
+  prm.Hkv = Hkv;
+  prm.M = M;
+  prm.N = N;
+  prm.G = Hq / Hkv;
+  prm.n_qtiles = (M + kBM - 1) / kBM;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.causal = causal ? 1 : 0;
+  prm.o = o;
+  prm.o_sb = o_strides[0];
+  prm.o_sh = o_strides[1];
+  prm.o_sm = o_strides[2];
+  prm.cos = rope_cos;
+  prm.sin = rope_sin;
+  prm.rope_max_pos = rope_max_pos;
+  prm.rope_q_pos0 = rope_q_pos0;
+
+  CUtensorMap mq, mk, mv;
+  int rc;
+  // a zero-length key axis still needs a valid map; it is never read (n_kv == 0)
+  const int n_map = N > 0 ? N : 1;
+  if ((rc = make_map(&mq, q, d, M, Hq, B, q_strides, bf16, "cie_prefill_attn(q)")) != CIE_OK)
+    return rc;
+  if ((rc = make_map(&mk, kk, d, n_map, Hkv, B, ks, bf16, "cie_prefill_attn(k)")) != CIE_OK)
+    return rc;
+  if ((rc = make_map(&mv, v, d, n_map, Hkv, B, v_strides, bf16, "cie_prefill_attn(v)")) !=
+      CIE_OK)
+    return rc;
+  if (d == 64)
+    return bf16 ? launch_prefill<64, true>(mq, mk, mv, prm, st)
+                : launch_prefill<64, false>(mq, mk, mv, prm, st);
+  return bf16 ? launch_prefill<128, true>(mq, mk, mv, prm, st)
+              : launch_prefill<128, false>(mq, mk, mv, prm, st);
+}

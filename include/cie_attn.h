@@ -1,0 +1,175 @@
+/*
+ * cie_attn.h — C ABI of libcie_attn.so, the B200 (sm_100a) attention hot path
+ * of the Custom-Inference-Engine LLM engine.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor pointers are CUDA device pointers owned by the caller.
+ *     The library never allocates device memory; scratch space is passed in
+ *     through `workspace` with a size obtained from the matching *_workspace()
+ *     query.
+ *   - Work is enqueued asynchronously on `stream` (a cudaStream_t, NULL = the
+ *     legacy default stream). A return value of CIE_OK means the launch was
+ *     accepted; device-side faults that the kernels detect themselves (bad
+ *     block ids, a pipeline wait that ran out of time) are recorded in a
+ *     per-device status word read by cie_device_status().
+ *   - Element type codes: CIE_DTYPE_BF16 or CIE_DTYPE_FP16 (Q, K, V, O and the
+ *     paged pools share one type). RoPE tables are fp32.
+ *   - Strides are in elements; the innermost (head_dim) stride must be 1.
+ *   - Every call is thread-safe: TMA descriptors are built per call on the
+ *     host stack and the only shared host state is a once-initialised driver
+ *     entry point.
+ */
+#ifndef CIE_ATTN_H_
+#define CIE_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum cie_status {
+  CIE_OK = 0,
+  CIE_ERR_INVALID = -1,      /* bad argument (shape, stride, alignment, dtype) */
+  CIE_ERR_UNSUPPORTED = -2,  /* valid but not implemented (e.g. head_dim 96)   */
+  CIE_ERR_WORKSPACE = -3,    /* workspace NULL or smaller than required        */
+  CIE_ERR_LAUNCH = -4,       /* CUDA launch / driver error                     */
+  CIE_ERR_DEVICE = -5        /* device-side status word is non-zero            */
+};
+
+enum cie_dtype { CIE_DTYPE_BF16 = 0, CIE_DTYPE_FP16 = 1 };
+
+/* Device status bits (cie_device_status). */
+#define CIE_DEV_BAD_BLOCK_ID 0x1  /* a block-table entry was < 0 or >= num_blocks */
+#define CIE_DEV_TIMEOUT 0x2       /* a bounded pipeline wait expired               */
+#define CIE_DEV_BAD_POSITION 0x4  /* a RoPE position fell outside the cos/sin table */
+
+/*
+ * Dense causal / non-causal grouped-query attention (prefill).
+ *
+ * Replaces the Triton launch in kernels/flash_attention.py:136-209
+ * (`flash_attention(q, k, v, causal, scale)`, grid at :175-208) and the GQA
+ * expansion at :152-155, which this kernel does not need (kv head = q head /
+ * (Hq / Hkv)).
+ *
+ *   q: (B, Hq, M, d)   k, v: (B, Hkv, N, d)   o: (B, Hq, M, d)
+ *   *_strides[0..2] = strides of the B, H and sequence dims (elements).
+ *   causal: bottom-right aligned, query i sees keys j <= N - M + i
+ *           (kernels/ref/flash_attention_ref.py:44-49).
+ *   rope_cos / rope_sin: optional fp32 (rope_max_pos, d/2) tables built as in
+ *           kernels/ref/rope_apply_ref.py:6-19. When non-NULL, q row i is
+ *           rotated at position rope_q_pos0 + i inside the kernel, and when
+ *           rope_k != 0, K row j is rotated at position j (half-split rotation,
+ *           kernels/ref/rope_apply_ref.py:49-53) into the workspace first.
+ *   d: 16, 32, 64, 128 or 256 (the reference accepts powers of two >= 16,
+ *      kernels/flash_attention.py:160-163). d in {64, 128} with more than 64
+ *      query rows per kv head runs on the tcgen05 kernel; everything else on
+ *      the split-KV mma.sync kernel over dense K/V.
+ */
+int cie_prefill_attn(const void* q, const void* k, const void* v, void* o,
+                     int B, int Hq, int Hkv, int M, int N, int d,
+                     const int64_t* q_strides, const int64_t* k_strides,
+                     const int64_t* v_strides, const int64_t* o_strides,
+                     float scale, int causal, int dtype,
+                     const float* rope_cos, const float* rope_sin,
+                     int rope_max_pos, int rope_q_pos0, int rope_k,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace cie_prefill_attn needs for these arguments: the
+ * rotated copy of K when rope_k is set, plus split-KV partials when the call
+ * is served by the short-query kernel (G*M <= 64, or d not 64/128). */
+size_t cie_prefill_attn_workspace(int B, int Hq, int Hkv, int M, int N, int d,
+                                  int dtype, int rope_k);
+
+/*
+ * Paged-KV attention for single-token decode (M = 1) and speculative verify
+ * (M = gamma + 1), reading K/V straight from the paged pools through the
+ * block table. Replaces the dense history gather of
+ * engine/cache/kv_cache.py:141-165 followed by flash_attention() at
+ * engine/model/block.py:65-71, for every sequence of a batch at once.
+ *
+ *   q:            (B, Hq, M, d) with q_strides (B, H, M dims, elements)
+ *   k_pool/v_pool:(num_blocks, block_size, Hkv, d) contiguous
+ *                 (engine/cache/kv_cache.py:34-64 layout)
+ *   block_tables: int32 (B, max_blocks); row b lists physical block ids in
+ *                 logical order (engine/cache/block_table.py:6-36)
+ *   kv_lens:      int32 (B,); kv_lens[b] tokens of history including the M
+ *                 query tokens, so query i sits at position kv_lens[b]-M+i.
+ *   o:            (B, Hq, M, d) with o_strides.
+ *   causal:       bottom-right aligned as above.
+ *   rope_cos/sin: optional; when non-NULL q row i is rotated at position
+ *                 kv_lens[b] - M + i (K is stored pre-rotated in the pool).
+ *   split_tokens: 0 = automatic; else tokens per split-KV partition (multiple
+ *                 of 16). Partitions are merged by a log-sum-exp kernel.
+ */
+int cie_paged_attn(const void* q, const void* k_pool, const void* v_pool,
+                   const int32_t* block_tables, const int32_t* kv_lens,
+                   void* o, int B, int Hq, int Hkv, int M, int d,
+                   int num_blocks, int block_size, int max_blocks,
+                   const int64_t* q_strides, const int64_t* o_strides,
+                   float scale, int causal, int dtype,
+                   const float* rope_cos, const float* rope_sin,
+                   int rope_max_pos, int split_tokens,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace cie_paged_attn needs for these arguments. */
+size_t cie_paged_attn_workspace(int B, int Hq, int Hkv, int M, int d,
+                                int block_size, int max_blocks,
+                                int split_tokens);
+
+/*
+ * Bit-exact gather of the paged history into a dense buffer:
+ *   out[b, t, h, :] = pool[block_tables[b, t / block_size], t % block_size, h, :]
+ * for t < kv_lens[b]; rows t >= kv_lens[b] (up to out_len) are left as they
+ * are. Mirrors PagedKVCache.gather (engine/cache/kv_cache.py:141-165) for a
+ * batch of sequences. out: (B, out_len, Hkv, d) contiguous.
+ */
+int cie_gather_kv(const void* pool, const int32_t* block_tables,
+                  const int32_t* kv_lens, void* out, int B, int out_len,
+                  int Hkv, int d, int num_blocks, int block_size,
+                  int max_blocks, int dtype, void* stream);
+
+/*
+ * Fused RoPE-on-K + paged append. For every new token (b, i), i < L:
+ *   pos = start_pos[b] + i
+ *   k_pool[blk, off, h, :] = rope(k_new[b, i, h, :], pos)   (if rope_cos)
+ *   v_pool[blk, off, h, :] = v_new[b, i, h, :]
+ * with (blk, off) = (block_tables[b, pos / block_size], pos % block_size).
+ * Replaces rope.apply(k) (engine/model/block.py:53-54) and the block-walked
+ * slice copies of PagedKVCache.append (engine/cache/kv_cache.py:102-139).
+ * k_new / v_new: (B, L, Hkv, d) with strides (elements) for the B, L, H dims.
+ */
+int cie_rope_append(const void* k_new, const void* v_new, void* k_pool,
+                    void* v_pool, const int32_t* block_tables,
+                    const int32_t* start_pos, int B, int L, int Hkv, int d,
+                    int num_blocks, int block_size, int max_blocks,
+                    const int64_t* kv_strides, int dtype,
+                    const float* rope_cos, const float* rope_sin,
+                    int rope_max_pos, void* stream);
+
+/*
+ * Standalone half-split RoPE: y[b, h, i, :] = rope(x[b, h, i, :], pos0 + i),
+ * computed in fp32 and rounded to the element type
+ * (kernels/ref/rope_apply_ref.py:22-53). x, y: (B, H, L, d) with strides.
+ */
+int cie_rope(const void* x, void* y, int B, int H, int L, int d,
+             const int64_t* x_strides, const int64_t* y_strides, int pos0,
+             int dtype, const float* rope_cos, const float* rope_sin,
+             int rope_max_pos, void* stream);
+
+/* Per-device status word (CIE_DEV_* bits) of the current device. Synchronizes
+ * `stream`. If clear != 0 the word is reset to 0 afterwards. */
+int cie_device_status(int* status_out, int clear, void* stream);
+
+/* Copies the last host-side error message of the calling thread into buf. */
+int cie_get_last_error(char* buf, int buf_len);
+
+/* Library version string, e.g. "cie_attn 0.1.0 sm_100a". */
+const char* cie_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CIE_ATTN_H_ */
