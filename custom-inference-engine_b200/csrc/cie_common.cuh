@@ -3,6 +3,7 @@
 // checking helpers used by every C-ABI entry point.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -53,6 +54,16 @@ inline int num_sms() {
   }
   return n > 0 ? n : 148;
 }
+
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                      const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                      const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                      CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver, resolved once through the runtime
+// (no link-time dependency on libcuda); nullptr if unavailable.
+PFN_encodeTiled_t tensor_map_encoder();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -1,5 +1,6 @@
 // paged_attn.cu — paged-KV attention for single-token decode and speculative
-// verify on sm_100a.
+// verify on sm_100a (and the same kernel over dense K/V for short query
+// blocks and head dims the tcgen05 prefill kernel does not take).
 //
 // What it computes (per sequence b, query head h, query row i < M):
 //   out[b,h,i,:] = softmax_j(q_rot[b,h,i,:] . K[b,kvh,j,:] * scale) V[b,kvh,j,:]
@@ -9,14 +10,22 @@
 // attention matches kernels/ref/flash_attention_ref.py:8-56 with GQA
 // (kv head = h / (Hq / Hkv)).
 //
-// How: one CTA per (split-KV partition, kv head, row group, sequence).
-// The query rows of all heads sharing a kv head (G = Hq/Hkv heads x M rows)
-// form the M side of m16n8k16 tensor-core MMAs, so K/V bytes are read from
-// HBM exactly once per kv head. Each of the 4 warps streams its own 16-token
-// K/V tiles with 16-byte cp.async (block-table lookup per row) through a
-// private multi-stage shared-memory ring, runs an online softmax with quad
-// shuffles, and the warps are merged in shared memory at the end. Partitions
-// of one sequence are merged by a log-sum-exp kernel.
+// How: one CTA per (split-KV partition, kv head, row group, sequence). The
+// query rows of all heads sharing a kv head (G = Hq/Hkv heads x M rows) form
+// the M side of m16n8k16 tensor-core MMAs, so K/V bytes are read from HBM once
+// per kv head. Each of the 4 warps streams its own 16-token K/V tiles through
+// a private ring of shared-memory stages:
+//   * TMA path (block size a multiple of 16, or dense K/V): one elected lane
+//     issues one 2-D box per 64-column slice of a 16-token block, completion
+//     tracked by an mbarrier per stage; no per-row address arithmetic.
+//   * cp.async path (any other block size): 16-byte cp.async per row chunk
+//     with a block-table lookup per row.
+// Both land tiles in the 16-byte-chunk XOR-swizzled layout TMA produces for
+// 32/64/128-byte rows, which ldmatrix reads without bank conflicts. Each warp
+// runs an online softmax (quad shuffles) over its tiles; the 4 warps are
+// merged in shared memory, and split-KV partitions of one sequence by a
+// log-sum-exp merge kernel.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cfloat>
@@ -50,10 +59,10 @@ struct PagedParams {
   float scale_log2;
   int causal;
   // dense mode (K/V as (B, Hkv, N, d) tensors instead of paged pools)
-  int dense_n;                       // N (keys per sequence)
-  int64_t k_sb, k_sh, k_sn;          // element strides of K
-  int64_t v_sb, v_sh, v_sn;          // element strides of V
-  int rope_q_pos0;                   // dense mode: q row i rotated at rope_q_pos0 + i
+  int dense_n;
+  int64_t k_sb, k_sh, k_sn;
+  int64_t v_sb, v_sh, v_sn;
+  int rope_q_pos0;  // dense mode: q row i rotated at rope_q_pos0 + i
 };
 
 constexpr int kPagedWarps = 4;
@@ -61,43 +70,65 @@ constexpr int kTileTok = 16;
 
 template <int D>
 struct PagedCfg {
-  static constexpr int kChunks = D / 8;  // 16-byte chunks per row
+  static constexpr int ROWB = (D * 2 < 128) ? D * 2 : 128;  // bytes per swizzled sub-row
+  static constexpr int KCS = ROWB / 16;                     // 16B chunks per sub-row
+  static constexpr int SUBS = (D * 2) / ROWB;               // 64-column slices per row
   static constexpr int kStages = (D <= 64) ? 4 : (D == 128 ? 3 : 2);
-  static constexpr int kTileBytes = kTileTok * D * 2;           // K or V tile
-  static constexpr int kStageBytes = 2 * kTileBytes;            // K + V
+  static constexpr int kTileBytes = kTileTok * D * 2;  // K or V tile
+  static constexpr int kStageBytes = 2 * kTileBytes;   // K + V
   static constexpr int kWarpBytes = kStages * kStageBytes;
   static constexpr int kPipeBytes = kPagedWarps * kWarpBytes;
 };
 
-// 16-byte-chunk XOR swizzle of a [rows][KC chunks] tile so that the 8 rows
-// an ldmatrix phase reads land in 8 distinct 16-byte bank groups.
+// 16-byte-chunk XOR swizzle of rows of KC chunks: the layout TMA writes for
+// 32/64/128-byte swizzle modes, so the 8 rows an ldmatrix phase reads land in
+// 8 distinct 16-byte bank groups.
 template <int KC>
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   if constexpr (KC >= 8) return static_cast<uint32_t>(chunk ^ (row & 7));
   else return static_cast<uint32_t>(chunk ^ ((row / (8 / KC)) & (KC - 1)));
 }
 
+// Byte offset of 16-byte chunk `ch` of tile row `row` in a K/V tile:
+// [SUBS][16 rows][ROWB], each slice swizzled.
+template <int D>
+__device__ __forceinline__ uint32_t kv_off(int row, int ch) {
+  using C = PagedCfg<D>;
+  const int sub = ch / C::KCS, w = ch % C::KCS;
+  return sub * (kTileTok * C::ROWB) + row * C::ROWB + swz<C::KCS>(row, w) * 16;
+}
+
 template <int D, int MT>
-__host__ __device__ constexpr int paged_smem_bytes() {
-  // pipeline ring, reused for the cross-warp merge, plus the rotated Q tile
+__host__ __device__ constexpr int paged_pipe_or_merge() {
   constexpr int RG = 16 * MT;
   constexpr int pipe = PagedCfg<D>::kPipeBytes;
   constexpr int merge = kPagedWarps * RG * (D + 2) * 4;
-  return (pipe > merge ? pipe : merge) + RG * D * 2;
+  return pipe > merge ? pipe : merge;
 }
 
-template <int D, int MT, bool BF16, bool PAGED>
+template <int D, int MT>
+__host__ __device__ constexpr int paged_smem_bytes() {
+  // pipeline ring (reused for the cross-warp merge) + rotated Q tile + barriers
+  return paged_pipe_or_merge<D, MT>() + 16 * MT * D * 2 +
+         kPagedWarps * PagedCfg<D>::kStages * 8 + 16 + 1024;
+}
+
+template <int D, int MT, bool BF16, bool PAGED, bool TMA>
 __global__ void __launch_bounds__(kPagedWarps * 32)
-    paged_attn_kernel(const PagedParams p) {
+    paged_attn_kernel(const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const PagedParams p) {
   using Cfg = PagedCfg<D>;
   constexpr int RG = 16 * MT;
-  constexpr int KC = Cfg::kChunks;
+  constexpr int KC = D / 8;
   constexpr int STAGES = Cfg::kStages;
 
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* pipe = smem;
-  const int pipe_or_merge = paged_smem_bytes<D, MT>() - RG * D * 2;
-  uint8_t* qs = smem + pipe_or_merge;
+  uint8_t* qs = smem + paged_pipe_or_merge<D, MT>();
+  uint64_t* full_bars = reinterpret_cast<uint64_t*>(qs + RG * D * 2);  // [warps][STAGES]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full_bars + kPagedWarps * STAGES);
 
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / p.row_groups;
@@ -111,13 +142,13 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
   if (kv_len < 0) kv_len = 0;
   if (PAGED && kv_len > p.max_blocks * p.block_size) {
     // a length beyond the table's capacity cannot be served: flag it and clamp
-    if (split == 0 && blockIdx.y == 0 && threadIdx.x == 0) raise_status(CIE_DEV_BAD_BLOCK_ID);
+    if (split == 0 && blockIdx.y == 0 && tid == 0) raise_status(CIE_DEV_BAD_BLOCK_ID);
     kv_len = p.max_blocks * p.block_size;
   }
   const int nsplit = kv_len > 0 ? (kv_len + p.split_tokens - 1) / p.split_tokens : 1;
   if (split >= nsplit) return;
-  const int R = p.G * p.M;            // rows of this kv-head group
-  const int row0 = rg * RG;           // first row of this CTA
+  const int R = p.G * p.M;   // rows of this kv-head group
+  const int row0 = rg * RG;  // first row of this CTA
   // keys past the last visible key of this CTA's rows are never loaded
   int key_cap = kv_len;
   if (p.causal) {
@@ -130,7 +161,15 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
   const int n_tiles = tok_end > tok_begin ? (tok_end - tok_begin + kTileTok - 1) / kTileTok : 0;
   const int q_pos_base = PAGED ? kv_len - p.M : p.rope_q_pos0;
 
-  // ---- rotated Q tile -> shared memory (bf16/fp16, 16B-chunk swizzle) ----
+  if constexpr (TMA) {
+    if (tid == 0) {
+      for (int i = 0; i < kPagedWarps * STAGES; ++i) mbar_init(full_bars + i, 1);
+      *abort_flag = 0;
+      fence_mbar_init();
+    }
+  }
+
+  // ---- rotated Q tile -> shared memory (16B-chunk swizzle) ----
   {
     using elem_t = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     const elem_t* q = reinterpret_cast<const elem_t*>(p.q);
@@ -145,8 +184,8 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
         const int gh = gr / p.M, m = gr % p.M;
         const int h = kvh * p.G + gh;
         const elem_t* src = q + b * p.q_sb + h * p.q_sh + m * p.q_sm;
-        uint4 x1 = *reinterpret_cast<const uint4*>(src + pc * 8);
-        uint4 x2 = *reinterpret_cast<const uint4*>(src + HALF + pc * 8);
+        const uint4 x1 = *reinterpret_cast<const uint4*>(src + pc * 8);
+        const uint4 x2 = *reinterpret_cast<const uint4*>(src + HALF + pc * 8);
         if (p.cos != nullptr) {
           int pos = q_pos_base + m;
           if (pos < 0 || pos >= p.rope_max_pos) {
@@ -166,12 +205,10 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
             const float c0 = cr[2 * e], c1 = cr[2 * e + 1];
             const float s0 = sr[2 * e], s1 = sr[2 * e + 1];
             // rot1 = x1*c - x2*s ; rot2 = x1*s + x2*c  (rope_apply_ref.py:49-53)
-            const float r10 = __fsub_rn(__fmul_rn(u1.x, c0), __fmul_rn(u2.x, s0));
-            const float r11 = __fsub_rn(__fmul_rn(u1.y, c1), __fmul_rn(u2.y, s1));
-            const float r20 = __fadd_rn(__fmul_rn(u1.x, s0), __fmul_rn(u2.x, c0));
-            const float r21 = __fadd_rn(__fmul_rn(u1.y, s1), __fmul_rn(u2.y, c1));
-            lo_w[e] = pack2<BF16>(r10, r11);
-            hi_w[e] = pack2<BF16>(r20, r21);
+            lo_w[e] = pack2<BF16>(__fsub_rn(__fmul_rn(u1.x, c0), __fmul_rn(u2.x, s0)),
+                                  __fsub_rn(__fmul_rn(u1.y, c1), __fmul_rn(u2.y, s1)));
+            hi_w[e] = pack2<BF16>(__fadd_rn(__fmul_rn(u1.x, s0), __fmul_rn(u2.x, c0)),
+                                  __fadd_rn(__fmul_rn(u1.y, s1), __fmul_rn(u2.y, c1)));
           }
         } else {
           lo = x1;
@@ -179,8 +216,8 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
         }
       }
       const int c_lo = pc, c_hi = HALF / 8 + pc;
-      *reinterpret_cast<uint4*>(qs + r * (D * 2) + swz<D / 8>(r, c_lo) * 16) = lo;
-      *reinterpret_cast<uint4*>(qs + r * (D * 2) + swz<D / 8>(r, c_hi) * 16) = hi;
+      *reinterpret_cast<uint4*>(qs + r * (D * 2) + swz<KC>(r, c_lo) * 16) = lo;
+      *reinterpret_cast<uint4*>(qs + r * (D * 2) + swz<KC>(r, c_hi) * 16) = hi;
     }
   }
   __syncthreads();
@@ -202,63 +239,108 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
   }
 
   uint8_t* wpipe = pipe + warp * Cfg::kWarpBytes;
+  uint64_t* wbars = full_bars + warp * STAGES;
   const int32_t* table = PAGED ? p.block_tables + static_cast<int64_t>(b) * p.max_blocks : nullptr;
   const uint8_t* kpool = reinterpret_cast<const uint8_t*>(p.k_pool);
   const uint8_t* vpool = reinterpret_cast<const uint8_t*>(p.v_pool);
   const int64_t tok_stride = static_cast<int64_t>(p.Hkv) * D * 2;  // bytes per token row
   const int64_t head_off = static_cast<int64_t>(kvh) * D * 2;
 
+  // physical block of the 16-token tile starting at t0 (TMA path: one block
+  // holds the whole tile); -1 when the table entry is invalid
+  auto tile_block = [&](int t0) -> int {
+    const int lb = t0 / p.block_size;
+    const int blk = lb < p.max_blocks ? table[lb] : -1;
+    return (blk < 0 || blk >= p.num_blocks) ? -1 : blk;
+  };
+
   auto issue_tile = [&](int tile, int stage) {
     uint8_t* ks = wpipe + stage * Cfg::kStageBytes;
     uint8_t* vs = ks + Cfg::kTileBytes;
     const int t0 = tok_begin + tile * kTileTok;
-#pragma unroll
-    for (int i = 0; i < (kTileTok * KC) / 32; ++i) {
-      const int q = lane + 32 * i;
-      const int row = q / KC;
-      const int ch = q % KC;
-      const int tok = t0 + row;
-      bool valid = tok < tok_end;
-      int64_t koff = 0, voff = 0;
-      if (valid) {
+    if constexpr (TMA) {
+      if (lane == 0) {
+        fence_proxy_async_smem();  // this warp's reads of the stage precede the overwrite
+        int c2 = 0, c3 = 0;
+        bool ok = true;
         if constexpr (PAGED) {
-          const int lb = tok / p.block_size;
-          const int blk = lb < p.max_blocks ? table[lb] : -1;
-          if (blk < 0 || blk >= p.num_blocks) {
-            raise_status(CIE_DEV_BAD_BLOCK_ID);
-            valid = false;
-          } else {
-            koff = (static_cast<int64_t>(blk) * p.block_size + (tok % p.block_size)) * tok_stride +
-                   head_off + ch * 16;
-            voff = koff;
+          const int blk = tile_block(t0);
+          ok = blk >= 0;
+          c2 = blk * p.block_size + (t0 % p.block_size);
+        } else {
+          c2 = kvh;
+          c3 = b;
+        }
+        if (ok) {
+          mbar_arrive_expect_tx(wbars + stage, 2 * Cfg::kTileBytes);
+#pragma unroll
+          for (int sub = 0; sub < Cfg::SUBS; ++sub) {
+            if constexpr (PAGED) {
+              tma_load_4d(ks + sub * kTileTok * Cfg::ROWB, &tm_k, wbars + stage, sub * 64, kvh,
+                          c2, 0);
+              tma_load_4d(vs + sub * kTileTok * Cfg::ROWB, &tm_v, wbars + stage, sub * 64, kvh,
+                          c2, 0);
+            } else {
+              tma_load_4d(ks + sub * kTileTok * Cfg::ROWB, &tm_k, wbars + stage, sub * 64, t0,
+                          c2, c3);
+              tma_load_4d(vs + sub * kTileTok * Cfg::ROWB, &tm_v, wbars + stage, sub * 64, t0,
+                          c2, c3);
+            }
           }
         } else {
-          koff = (b * p.k_sb + kvh * p.k_sh + tok * p.k_sn) * 2 + ch * 16;
-          voff = (b * p.v_sb + kvh * p.v_sh + tok * p.v_sn) * 2 + ch * 16;
+          raise_status(CIE_DEV_BAD_BLOCK_ID);
+          mbar_arrive(wbars + stage);  // completes the phase; the stage is zeroed on use
         }
       }
-      const uint32_t so = row * (D * 2) + swz<KC>(row, ch) * 16;
-      cp_async_16(ks + so, kpool + koff, valid);
-      cp_async_16(vs + so, vpool + voff, valid);
+    } else {
+#pragma unroll
+      for (int i = 0; i < (kTileTok * KC) / 32; ++i) {
+        const int q = lane + 32 * i;
+        const int row = q / KC;
+        const int ch = q % KC;
+        const int tok = t0 + row;
+        bool valid = tok < tok_end;
+        int64_t koff = 0, voff = 0;
+        if (valid) {
+          if constexpr (PAGED) {
+            const int lb = tok / p.block_size;
+            const int blk = lb < p.max_blocks ? table[lb] : -1;
+            if (blk < 0 || blk >= p.num_blocks) {
+              raise_status(CIE_DEV_BAD_BLOCK_ID);
+              valid = false;
+            } else {
+              koff = (static_cast<int64_t>(blk) * p.block_size + (tok % p.block_size)) *
+                         tok_stride + head_off + ch * 16;
+              voff = koff;
+            }
+          } else {
+            koff = (b * p.k_sb + kvh * p.k_sh + tok * p.k_sn) * 2 + ch * 16;
+            voff = (b * p.v_sb + kvh * p.v_sh + tok * p.v_sn) * 2 + ch * 16;
+          }
+        }
+        const uint32_t so = kv_off<D>(row, ch);
+        cp_async_16(ks + so, kpool + koff, valid);
+        cp_async_16(vs + so, vpool + voff, valid);
+      }
     }
   };
 
   // Q A-fragments (held in registers when small).
   constexpr bool kQReg = (MT * D) <= 128;
   uint32_t qa[kQReg ? MT : 1][kQReg ? D / 16 : 1][4];
-  auto load_qfrag = [&](int mt, int ks, uint32_t (&a)[4]) {
+  auto load_qfrag = [&](int mt, int kk, uint32_t (&a)[4]) {
     const int row = mt * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
-    const int ch = 2 * ks + (lane >> 4);
+    const int ch = 2 * kk + (lane >> 4);
     ldmatrix_x4(smem_u32(qs + row * (D * 2) + swz<KC>(row, ch) * 16), a[0], a[1], a[2], a[3]);
   };
   if constexpr (kQReg) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) load_qfrag(mt, ks, qa[mt][ks]);
+      for (int kk = 0; kk < D / 16; ++kk) load_qfrag(mt, kk, qa[mt][kk]);
   }
 
-  // Rows owned by this thread: (mt, half) -> global row / query index / key limit
+  // Key limit of each row this thread owns: (mt, half) -> keys <= lim are visible
   int lim[MT][2];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
@@ -271,24 +353,57 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
   const int lim_min = p.causal ? (kv_len - p.M) : (kv_len - 1);
 
   const int my_tiles = n_tiles > warp ? (n_tiles - warp + kPagedWarps - 1) / kPagedWarps : 0;
+  int issued = 0;
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
-    if (s < my_tiles) issue_tile(warp + kPagedWarps * s, s);
-    cp_async_commit();
+    if (s < my_tiles) {
+      issue_tile(warp + kPagedWarps * s, s);
+      ++issued;
+    }
+    if constexpr (!TMA) cp_async_commit();
   }
 
   for (int it = 0; it < my_tiles; ++it) {
     {
       const int nx = it + STAGES - 1;
-      if (nx < my_tiles) issue_tile(warp + kPagedWarps * nx, nx % STAGES);
-      cp_async_commit();
+      if (nx < my_tiles) {
+        issue_tile(warp + kPagedWarps * nx, nx % STAGES);
+        ++issued;
+      }
+      if constexpr (!TMA) cp_async_commit();
     }
-    cp_async_wait<STAGES - 1>();
-    __syncwarp();
-
-    const uint8_t* ks = wpipe + (it % STAGES) * Cfg::kStageBytes;
-    const uint8_t* vs = ks + Cfg::kTileBytes;
+    const int stage = it % STAGES;
+    uint8_t* ks = wpipe + stage * Cfg::kStageBytes;
+    uint8_t* vs = ks + Cfg::kTileBytes;
     const int t0 = tok_begin + (warp + kPagedWarps * it) * kTileTok;
+    if constexpr (TMA) {
+      const bool ok = mbar_wait_bounded(wbars + stage, (it / STAGES) & 1, abort_flag, kWaitLimitNs);
+      if (!__all_sync(0xffffffffu, ok)) {
+        raise_status(CIE_DEV_TIMEOUT);
+        break;
+      }
+      // rows past the valid keys of a paged tile hold whatever the block holds:
+      // zero them in V (P is 0 there, but 0 * NaN would not be); a tile whose
+      // block id was refused is zeroed entirely
+      int valid_rows = kTileTok;
+      if constexpr (PAGED) {
+        if (tile_block(t0) < 0) valid_rows = 0;
+        else if (t0 + kTileTok > kv_len) valid_rows = kv_len - t0;
+      }
+      if (valid_rows < kTileTok) {
+        for (int q = lane; q < kTileTok * KC; q += 32) {
+          const int row = q / KC, ch = q % KC;
+          if (row >= valid_rows) {
+            *reinterpret_cast<uint4*>(vs + kv_off<D>(row, ch)) = make_uint4(0, 0, 0, 0);
+            if (valid_rows == 0)
+              *reinterpret_cast<uint4*>(ks + kv_off<D>(row, ch)) = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
+    } else {
+      cp_async_wait<STAGES - 1>();
+    }
+    __syncwarp();
 
     // S = Q K^T over 16 tokens (2 n-tiles of 8)
     float s[MT][2][4];
@@ -304,7 +419,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
       {
         const int row = (lane & 7) + ((lane >> 4) << 3);
         const int ch = 2 * kk + ((lane >> 3) & 1);
-        ldmatrix_x4(smem_u32(ks + row * (D * 2) + swz<KC>(row, ch) * 16), b0, b1, b2, b3);
+        ldmatrix_x4(smem_u32(ks + kv_off<D>(row, ch)), b0, b1, b2, b3);
       }
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
@@ -320,9 +435,11 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
       }
     }
 
-    // online softmax (log2 domain)
+    // online softmax (log2 domain); O is rescaled only when some row's max grew
     const bool need_mask = (t0 + kTileTok - 1) > lim_min;
     uint32_t pa[MT][4];
+    float alpha[MT][2];
+    bool any_rescale = false;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
@@ -344,7 +461,8 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         const float m_new = fmaxf(m_run[mt][hf], mx);
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = ex2(m_run[mt][hf] - m_use);
+        alpha[mt][hf] = ex2(m_run[mt][hf] - m_use);
+        any_rescale |= (m_new != m_run[mt][hf]);
         m_run[mt][hf] = m_new;
         float ps = 0.f;
 #pragma unroll
@@ -352,16 +470,22 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
           v[j] = ex2(v[j] - m_use);
           ps += v[j];
         }
-        l_run[mt][hf] = l_run[mt][hf] * alpha + ps;
-#pragma unroll
-        for (int nt = 0; nt < D / 8; ++nt) {
-          o_acc[mt][nt][2 * hf] *= alpha;
-          o_acc[mt][nt][2 * hf + 1] *= alpha;
-        }
+        l_run[mt][hf] = l_run[mt][hf] * alpha[mt][hf] + ps;
         // A fragment of P: a0/a1 = rows g/g+8, tokens 2t..2t+1; a2/a3 = tokens 8+2t..
         pa[mt][hf] = pack2<BF16>(v[0], v[1]);
         pa[mt][2 + hf] = pack2<BF16>(v[2], v[3]);
       }
+    }
+    if (__any_sync(0xffffffffu, any_rescale)) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < D / 8; ++nt) {
+          o_acc[mt][nt][0] *= alpha[mt][0];
+          o_acc[mt][nt][1] *= alpha[mt][0];
+          o_acc[mt][nt][2] *= alpha[mt][1];
+          o_acc[mt][nt][3] *= alpha[mt][1];
+        }
     }
 
     // O += P V
@@ -371,7 +495,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
       {
         const int row = (lane & 7) + (((lane >> 3) & 1) << 3);
         const int ch = 2 * nd + (lane >> 4);
-        ldmatrix_x4_trans(smem_u32(vs + row * (D * 2) + swz<KC>(row, ch) * 16), b0, b1, b2, b3);
+        ldmatrix_x4_trans(smem_u32(vs + kv_off<D>(row, ch)), b0, b1, b2, b3);
       }
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
@@ -381,13 +505,21 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
     }
     __syncwarp();
   }
-  cp_async_wait<0>();
+  if constexpr (TMA) {
+    if (*abort_flag && lane == 0) {
+      // drain this warp's copies still in flight before the stages are reused
+      for (int j = issued - 1; j >= 0 && j >= issued - STAGES; --j)
+        mbar_wait_timeout(wbars + (j % STAGES), (j / STAGES) & 1, kWaitLimitNs);
+    }
+  } else {
+    cp_async_wait<0>();
+  }
   __syncthreads();  // pipeline ring is reused below
 
   // ---- merge the 4 warps in shared memory ----
-  float* sm_o = reinterpret_cast<float*>(pipe);                   // [W][RG][D]
-  float* sm_m = sm_o + kPagedWarps * RG * D;                      // [W][RG]
-  float* sm_l = sm_m + kPagedWarps * RG;                          // [W][RG]
+  float* sm_o = reinterpret_cast<float*>(pipe);   // [W][RG][D]
+  float* sm_m = sm_o + kPagedWarps * RG * D;      // [W][RG]
+  float* sm_l = sm_m + kPagedWarps * RG;          // [W][RG]
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -443,44 +575,75 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
   }
 }
 
-// Log-sum-exp merge of split-KV partitions (only sequences with >1 split).
+// Log-sum-exp merge of split-KV partitions (sequences with >1 split only).
+// One CTA per (sequence, kv head, row group): row weights are computed once
+// into shared memory, then every thread combines float4 slices of the rows.
+constexpr int kMergeCap = 32;
+
 template <int D, int RG, bool BF16, bool PAGED>
-__global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
-  const int kvh = blockIdx.x / p.row_groups;
-  const int rg = blockIdx.x % p.row_groups;
-  const int b = blockIdx.y;
+__global__ void __launch_bounds__(256) paged_merge_kernel(const PagedParams p) {
+  __shared__ float s_w[RG][kMergeCap];
+  __shared__ float s_mx[RG];
+  __shared__ float s_inv[RG];
+  const int unit = blockIdx.x;
+  const int rg = unit % p.row_groups;
+  const int kvh = (unit / p.row_groups) % p.Hkv;
+  const int b = unit / (p.row_groups * p.Hkv);
   int kv_len = PAGED ? p.kv_lens[b] : p.dense_n;
   if (kv_len < 0) kv_len = 0;
   if (PAGED && kv_len > p.max_blocks * p.block_size) kv_len = p.max_blocks * p.block_size;
   const int nsplit = kv_len > 0 ? (kv_len + p.split_tokens - 1) / p.split_tokens : 1;
   if (nsplit <= 1) return;
   const int R = p.G * p.M;
-  const int unit = (b * p.Hkv + kvh) * p.row_groups + rg;
   const int64_t base = static_cast<int64_t>(unit) * p.max_splits * RG;
-  using elem_t = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  elem_t* o = reinterpret_cast<elem_t*>(p.o);
-  for (int idx = threadIdx.x; idx < RG * D; idx += blockDim.x) {
-    const int r = idx / D, d = idx % D;
-    const int gr = rg * RG + r;
-    if (gr >= R) continue;
+  for (int r = threadIdx.x; r < RG; r += blockDim.x) {
     float mx = -INFINITY;
     for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, p.part_lse[base + s * RG + r]);
-    float out;
-    if (mx == -INFINITY) {
-      out = __int_as_float(0x7fc00000);
-    } else {
-      float acc = 0.f, wsum = 0.f;
-      for (int s = 0; s < nsplit; ++s) {
-        const float w = ex2(p.part_lse[base + s * RG + r] - mx);
-        wsum += w;
-        acc += w * p.part_o[(base + s * RG + r) * D + d];
-      }
-      out = acc / wsum;
+    float sum = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float w = mx == -INFINITY ? 0.f : ex2(p.part_lse[base + s * RG + r] - mx);
+      if (s < kMergeCap) s_w[r][s] = w;
+      sum += w;
     }
+    s_mx[r] = mx;
+    s_inv[r] = sum > 0.f ? 1.0f / sum : __int_as_float(0x7fc00000);
+  }
+  __syncthreads();
+  using elem_t = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  elem_t* o = reinterpret_cast<elem_t*>(p.o);
+  constexpr int D4 = D / 4;
+  for (int idx = threadIdx.x; idx < RG * D4; idx += blockDim.x) {
+    const int r = idx / D4, c = idx % D4;
+    const int gr = rg * RG + r;
+    if (gr >= R) continue;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < nsplit; ++s) {
+      const float w = s < kMergeCap ? s_w[r][s]
+                                    : (s_mx[r] == -INFINITY
+                                           ? 0.f
+                                           : ex2(p.part_lse[base + s * RG + r] - s_mx[r]));
+      const float4 v =
+          *reinterpret_cast<const float4*>(p.part_o + (base + s * RG + r) * D + c * 4);
+      acc.x += w * v.x;
+      acc.y += w * v.y;
+      acc.z += w * v.z;
+      acc.w += w * v.w;
+    }
+    const float inv = s_inv[r];
     const int gh = gr / p.M, m = gr % p.M;
     const int h = kvh * p.G + gh;
-    if constexpr (BF16) o[b * p.o_sb + h * p.o_sh + m * p.o_sm + d] = __float2bfloat16_rn(out);
-    else o[b * p.o_sb + h * p.o_sh + m * p.o_sm + d] = __float2half_rn(out);
+    elem_t* dst = o + b * p.o_sb + h * p.o_sh + m * p.o_sm + c * 4;
+    if constexpr (BF16) {
+      dst[0] = __float2bfloat16_rn(acc.x * inv);
+      dst[1] = __float2bfloat16_rn(acc.y * inv);
+      dst[2] = __float2bfloat16_rn(acc.z * inv);
+      dst[3] = __float2bfloat16_rn(acc.w * inv);
+    } else {
+      dst[0] = __float2half_rn(acc.x * inv);
+      dst[1] = __float2half_rn(acc.y * inv);
+      dst[2] = __float2half_rn(acc.z * inv);
+      dst[3] = __float2half_rn(acc.w * inv);
+    }
   }
 }
 
@@ -493,12 +656,14 @@ static int pick_mt(int R, int d) {
 }
 
 static int auto_split_tokens(int64_t units, int max_len, int d) {
-  // aim for ~8 partitions of work per SM over the whole batch, each at least
-  // 256 tokens (512 for d >= 128), at most 4096, a multiple of 64 (one
-  // 16-token tile per warp)
+  // Lengths are only known on the device, so partitions are sized from the
+  // table width: about 32 (d <= 64) or 16 (d >= 128) partitions per SM over
+  // the batch if every sequence were full, never below 256 / 1024 tokens (so
+  // the partial-result traffic stays around 1% of the K/V bytes), at most 4096.
   const int sms = num_sms();
-  int64_t want = (static_cast<int64_t>(max_len) * units) / (static_cast<int64_t>(sms) * 8);
-  const int lo = (d >= 128) ? 512 : 256;
+  const int per_sm = d >= 128 ? 16 : 32;
+  int64_t want = (static_cast<int64_t>(max_len) * units) / (static_cast<int64_t>(sms) * per_sm);
+  const int lo = (d >= 128) ? 1024 : 256;
   if (want < lo) want = lo;
   if (want > 4096) want = 4096;
   want = ((want + 63) / 64) * 64;
@@ -532,20 +697,73 @@ static MmaPlan make_plan(int B, int Hq, int Hkv, int M, int d, int max_len, int 
 
 static bool mma_head_dim_ok(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
 
-template <int D, int MT, bool BF16, bool PAGED>
-static int launch_mma(const PagedParams& prm, cudaStream_t st) {
+// 4-D map whose box is one 16-token, min(d, 64)-column K or V slice, swizzled
+// as kv_off<> expects. dims / strides innermost first, strides in bytes.
+static bool make_kv_map(CUtensorMap* map, const void* base, int d, const cuuint64_t* dims,
+                        const cuuint64_t* strides, const cuuint32_t* box, bool bf16) {
+  PFN_encodeTiled_t enc = tensor_map_encoder();
+  if (!enc) return false;
+  const int rowb = d * 2 < 128 ? d * 2 : 128;
+  const CUtensorMapSwizzle sw = rowb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : rowb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                             : CU_TENSOR_MAP_SWIZZLE_32B;
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D, int MT, bool BF16, bool PAGED, bool TMA>
+static int launch_mma_t(const CUtensorMap& mk, const CUtensorMap& mv, const PagedParams& prm,
+                        cudaStream_t st) {
   constexpr int smem = paged_smem_bytes<D, MT>();
-  auto kern = paged_attn_kernel<D, MT, BF16, PAGED>;
+  auto kern = paged_attn_kernel<D, MT, BF16, PAGED, TMA>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid(prm.max_splits, prm.Hkv * prm.row_groups, prm.B);
-  kern<<<grid, kPagedWarps * 32, smem, st>>>(prm);
+  kern<<<grid, kPagedWarps * 32, smem, st>>>(mk, mv, prm);
   CIE_CHECK_LAUNCH("paged_attn_kernel");
   if (prm.max_splits > 1) {
-    dim3 mg(prm.Hkv * prm.row_groups, prm.B);
-    paged_merge_kernel<D, 16 * MT, BF16, PAGED><<<mg, 128, 0, st>>>(prm);
+    paged_merge_kernel<D, 16 * MT, BF16, PAGED>
+        <<<prm.B * prm.Hkv * prm.row_groups, 256, 0, st>>>(prm);
     CIE_CHECK_LAUNCH("paged_merge_kernel");
   }
   return CIE_OK;
+}
+
+template <int D, int MT, bool BF16, bool PAGED>
+static int launch_mma(const PagedParams& prm, cudaStream_t st) {
+  // TMA feeds need a 16-token tile inside one block (paged) and 16-byte
+  // aligned rows; otherwise the cp.async path serves the call.
+  using C = PagedCfg<D>;
+  CUtensorMap mk{}, mv{};
+  bool tma = false;
+  const bool bf16 = BF16;
+  if constexpr (PAGED) {
+    if (prm.block_size % kTileTok == 0) {
+      const cuuint64_t tokens = static_cast<cuuint64_t>(prm.num_blocks) * prm.block_size;
+      const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)prm.Hkv, tokens, 1};
+      const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)prm.Hkv * D * 2,
+                                     tokens * prm.Hkv * D * 2};
+      const cuuint32_t box[4] = {(cuuint32_t)(C::ROWB / 2), 1, kTileTok, 1};
+      tma = make_kv_map(&mk, prm.k_pool, D, dims, strides, box, bf16) &&
+            make_kv_map(&mv, prm.v_pool, D, dims, strides, box, bf16);
+    }
+  } else {
+    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)(prm.dense_n > 0 ? prm.dense_n : 1),
+                                (cuuint64_t)prm.Hkv, (cuuint64_t)prm.B};
+    const cuuint64_t ks[3] = {(cuuint64_t)prm.k_sn * 2, (cuuint64_t)prm.k_sh * 2,
+                              (cuuint64_t)prm.k_sb * 2};
+    const cuuint64_t vs[3] = {(cuuint64_t)prm.v_sn * 2, (cuuint64_t)prm.v_sh * 2,
+                              (cuuint64_t)prm.v_sb * 2};
+    const cuuint32_t box[4] = {(cuuint32_t)(C::ROWB / 2), kTileTok, 1, 1};
+    const bool ok_strides = prm.k_sn > 0 && prm.k_sh > 0 && prm.k_sb > 0 && prm.v_sn > 0 &&
+                            prm.v_sh > 0 && prm.v_sb > 0;
+    tma = ok_strides && make_kv_map(&mk, prm.k_pool, D, dims, ks, box, bf16) &&
+          make_kv_map(&mv, prm.v_pool, D, dims, vs, box, bf16);
+  }
+  if (tma) return launch_mma_t<D, MT, BF16, PAGED, true>(mk, mv, prm, st);
+  return launch_mma_t<D, MT, BF16, PAGED, false>(mk, mv, prm, st);
 }
 
 template <int D, bool BF16, bool PAGED>
@@ -553,7 +771,8 @@ static int dispatch_mt(const PagedParams& prm, int mt, cudaStream_t st) {
   if constexpr (D >= 256) {
     return launch_mma<D, 1, BF16, PAGED>(prm, st);
   } else if constexpr (D == 128) {
-    return mt == 1 ? launch_mma<D, 1, BF16, PAGED>(prm, st) : launch_mma<D, 2, BF16, PAGED>(prm, st);
+    return mt == 1 ? launch_mma<D, 1, BF16, PAGED>(prm, st)
+                   : launch_mma<D, 2, BF16, PAGED>(prm, st);
   } else {
     switch (mt) {
       case 1: return launch_mma<D, 1, BF16, PAGED>(prm, st);
@@ -566,11 +785,16 @@ static int dispatch_mt(const PagedParams& prm, int mt, cudaStream_t st) {
 template <bool PAGED>
 static int dispatch_d(const PagedParams& prm, int d, int mt, bool bf16, cudaStream_t st) {
   switch (d) {
-    case 16: return bf16 ? dispatch_mt<16, true, PAGED>(prm, mt, st) : dispatch_mt<16, false, PAGED>(prm, mt, st);
-    case 32: return bf16 ? dispatch_mt<32, true, PAGED>(prm, mt, st) : dispatch_mt<32, false, PAGED>(prm, mt, st);
-    case 64: return bf16 ? dispatch_mt<64, true, PAGED>(prm, mt, st) : dispatch_mt<64, false, PAGED>(prm, mt, st);
-    case 128: return bf16 ? dispatch_mt<128, true, PAGED>(prm, mt, st) : dispatch_mt<128, false, PAGED>(prm, mt, st);
-    case 256: return bf16 ? dispatch_mt<256, true, PAGED>(prm, mt, st) : dispatch_mt<256, false, PAGED>(prm, mt, st);
+    case 16: return bf16 ? dispatch_mt<16, true, PAGED>(prm, mt, st)
+                         : dispatch_mt<16, false, PAGED>(prm, mt, st);
+    case 32: return bf16 ? dispatch_mt<32, true, PAGED>(prm, mt, st)
+                         : dispatch_mt<32, false, PAGED>(prm, mt, st);
+    case 64: return bf16 ? dispatch_mt<64, true, PAGED>(prm, mt, st)
+                         : dispatch_mt<64, false, PAGED>(prm, mt, st);
+    case 128: return bf16 ? dispatch_mt<128, true, PAGED>(prm, mt, st)
+                          : dispatch_mt<128, false, PAGED>(prm, mt, st);
+    case 256: return bf16 ? dispatch_mt<256, true, PAGED>(prm, mt, st)
+                          : dispatch_mt<256, false, PAGED>(prm, mt, st);
     default:
       set_error("attention: head_dim %d unsupported", d);
       return CIE_ERR_UNSUPPORTED;
@@ -609,8 +833,8 @@ static void fill_common(PagedParams& prm, const MmaPlan& pl, const void* q, void
   prm.causal = causal ? 1 : 0;
 }
 
-// Dense-K/V variant of the same kernel, used by cie_prefill_attn for head
-// dims the tcgen05 kernel does not cover (16, 32, 256).
+// Dense-K/V variant of the same kernel, used by cie_prefill_attn for short
+// query blocks and for head dims the tcgen05 kernel does not cover.
 size_t dense_mma_workspace(int B, int Hq, int Hkv, int M, int N, int d) {
   return make_plan(B, Hq, Hkv, M, d, N, 0).workspace();
 }
@@ -629,6 +853,10 @@ int dense_mma_attn(const void* q, const void* k, const void* v, void* o, int B, 
     set_error("attention: workspace of %zu bytes required, got %zu", pl.workspace(),
               workspace_bytes);
     return CIE_ERR_WORKSPACE;
+  }
+  if (B > 65535 || static_cast<int64_t>(Hkv) * pl.row_groups > 65535) {
+    set_error("attention: grid too large (B=%d, Hkv*row_groups=%d)", B, Hkv * pl.row_groups);
+    return CIE_ERR_UNSUPPORTED;
   }
   PagedParams prm{};
   fill_common(prm, pl, q, o, B, Hq, Hkv, M, qs, os, scale, causal, cos, sin, max_pos, workspace);
@@ -692,6 +920,11 @@ extern "C" int cie_paged_attn(const void* q, const void* k_pool, const void* v_p
     set_error("cie_paged_attn: workspace of %zu bytes required, got %zu", pl.workspace(),
               workspace_bytes);
     return CIE_ERR_WORKSPACE;
+  }
+  if (B > 65535 || static_cast<int64_t>(Hkv) * pl.row_groups > 65535) {
+    set_error("cie_paged_attn: grid too large (B=%d, Hkv*row_groups=%d)", B,
+              Hkv * pl.row_groups);
+    return CIE_ERR_UNSUPPORTED;
   }
   PagedParams prm{};
   fill_common(prm, pl, q, o, B, Hq, Hkv, M, q_strides, o_strides, scale, causal, rope_cos,

@@ -420,30 +420,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 }
 
 // ------------------------------------------------------------------ host
-typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                    const cuuint32_t*, CUtensorMapInterleave,
-                                    CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                    CUtensorMapFloatOOBfill);
-
-static PFN_encodeTiled get_encode_fn() {
-  static PFN_encodeTiled fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, []() {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_encodeTiled>(ptr);
-  });
-  return fn;
-}
-
 // 4-D map over (d, seq, head, batch) with a (64, 128, 1, 1) box, 128B swizzle.
 static int make_map(CUtensorMap* map, const void* base, int d, int seq, int heads, int batch,
                     const int64_t* strides, bool bf16, const char* what) {
-  PFN_encodeTiled enc = get_encode_fn();
+  PFN_encodeTiled_t enc = tensor_map_encoder();
   if (!enc) {
     set_error("%s: cuTensorMapEncodeTiled unavailable", what);
     return CIE_ERR_LAUNCH;
