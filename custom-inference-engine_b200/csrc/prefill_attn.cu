@@ -5,25 +5,30 @@
 // and the Triton entry kernels/flash_attention.py:136-209: out = softmax(
 // q k^T * scale + bottom-right causal mask) v, with the kv head of q head h
 // being h / (Hq / Hkv) (no K/V expansion), optional half-split RoPE of q
-// applied to the Q tile in shared memory (kernels/ref/rope_apply_ref.py:22-53).
+// applied to the Q tiles in shared memory (kernels/ref/rope_apply_ref.py:22-53).
 //
-// One CTA owns a 128-row query tile of one (batch, head) and streams 128-key
-// K/V tiles:
-//   warp 0      TMA producer: Q once, then K_j / V_j into a ring of stages
-//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer:
-//                 S_j = Q K_j^T   (SS MMA, fp32 in TMEM, double-buffered)
-//                 O  += P_j V_j   (TS MMA, P read from TMEM, V MN-major)
-//   warps 2..5  softmax: thread r owns query row r == TMEM lane r, so row
-//               max / sum need no cross-thread reduction; writes P (16-bit)
-//               back to TMEM; rescales O in TMEM only when the running max
-//               grew by more than 2^8 (the stale max is exact because O and
-//               the row sum share it); epilogue O / l -> global.
-// Causal tiles are ordered heaviest first across the grid.
+// One CTA owns two 128-row query tiles (Q0, Q1) of one (batch, head) and
+// streams 128-key K/V tiles through a TMA ring shared by both:
+//   warp 0      TMA producer: Q0/Q1 once, then K_j / V_j into a ring of stages
+//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
+//   warps 4..7  softmax of tile 0, warps 8..11 softmax of tile 1: thread r owns
+//               query row r == TMEM lane r (row max / sum need no shuffles),
+//               writes P (16-bit) over its S columns in TMEM, rescales its O
+//               rows in TMEM only when the running max grew by more than 2^8
+//               (the stale max is exact because O and the row sum share it),
+//               and stores O / l at the end.
+// Tensor-core order per key tile j: PV0_j, S0_{j+1}, PV1_j, S1_{j+1}, so each
+// softmax warpgroup works on its tile while the tensor core serves the other
+// one. S_t accumulates in TMEM (fp32), P_t overwrites the first 64 columns of
+// S_t, O_t accumulates in TMEM. MMAs of one CTA execute in issue order, so
+// S_t{j+1} may be issued right behind PV_t_j that still reads P_t from the same
+// columns, and the commit that signals S_t_j complete also covers PV_t_{j-1},
+// which is what lets the softmax rescale O_t without a separate wait.
+// Causal tile pairs are ordered heaviest first across the grid.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
-#include <mutex>
 #include <type_traits>
 
 #include "cie_common.cuh"
@@ -31,26 +36,32 @@
 
 namespace cie {
 
-constexpr int kPfThreads = 192;
-constexpr int kBM = 128;
-constexpr int kBN = 128;
+constexpr int kPfThreads = 384;  // 3 warpgroups
+// Launched at 168 registers per thread (3 warps per scheduler); warpgroup 0
+// (producer, MMA issuer, 2 idle warps) gives registers to the two softmax
+// warpgroups: 48 + 224 + 224 = 496 <= 3 * 168 per scheduler.
+constexpr int kRegsCtrl = 48;
+constexpr int kRegsSoftmax = 224;
+constexpr int kBM = 128;         // rows of one query tile; a CTA owns two
+constexpr int kBN = 128;         // keys per K/V tile
 
 template <int D>
 struct PfCfg {
-  static constexpr int KCH = D / 64;                 // 128-byte swizzle chunks along d
+  static constexpr int KCH = D / 64;  // 128-byte swizzle chunks along d
   static constexpr int Q_BYTES = kBM * D * 2;
   static constexpr int KV_BYTES = kBN * D * 2;
   static constexpr int STAGES = (D == 64) ? 4 : 2;
-  static constexpr int BAR_OFF = Q_BYTES + 2 * STAGES * KV_BYTES;
-  static constexpr int NBARS = 2 + 4 * STAGES + 2 + 2 + 2 + 1 + 1;
+  static constexpr int BAR_OFF = 2 * Q_BYTES + 2 * STAGES * KV_BYTES;
+  static constexpr int NBARS = 2 + 4 * STAGES + 2 + 2 + 2 + 1;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 /*tmem slot, abort*/ + 1024 /*align*/;
-  static constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_P0 = 256, TM_P1 = 320, TM_O = 384;
+  static constexpr uint32_t TM_S0 = 0, TM_S1 = 128;    // P_t aliases cols [0, 64) of S_t
+  static constexpr uint32_t TM_O0 = 256, TM_O1 = 256 + D;
   static constexpr uint32_t TM_COLS = 512;
 };
 
 struct PrefillParams {
   int B, Hq, Hkv, M, N, G;
-  int n_qtiles;
+  int n_pairs;  // query tile pairs per (batch, head)
   float scale_log2;
   int causal;
   void* o;
@@ -62,6 +73,47 @@ struct PrefillParams {
 };
 
 template <int D, bool BF16>
+__device__ __forceinline__ void rope_q_row(uint8_t* sQt, int row, int pos, const float* cos,
+                                           const float* sin) {
+  constexpr int HALF = D / 2;
+  const float* cr = cos + static_cast<int64_t>(pos) * HALF;
+  const float* sr = sin + static_cast<int64_t>(pos) * HALF;
+#pragma unroll
+  for (int pc = 0; pc < HALF / 8; ++pc) {
+    const int e_lo = pc * 8, e_hi = HALF + pc * 8;
+    uint8_t* a_lo = sQt + (e_lo / 64) * kBM * 128 + row * 128 + ((((e_lo % 64) / 8) ^ (row & 7)) * 16);
+    uint8_t* a_hi = sQt + (e_hi / 64) * kBM * 128 + row * 128 + ((((e_hi % 64) / 8) ^ (row & 7)) * 16);
+    const uint4 x1 = *reinterpret_cast<uint4*>(a_lo);
+    const uint4 x2 = *reinterpret_cast<uint4*>(a_hi);
+    const float4 ca = *reinterpret_cast<const float4*>(cr + e_lo);
+    const float4 cb = *reinterpret_cast<const float4*>(cr + e_lo + 4);
+    const float4 sa = *reinterpret_cast<const float4*>(sr + e_lo);
+    const float4 sb = *reinterpret_cast<const float4*>(sr + e_lo + 4);
+    const float cc[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+    const float ss[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+    const uint32_t* u1 = reinterpret_cast<const uint32_t*>(&x1);
+    const uint32_t* u2 = reinterpret_cast<const uint32_t*>(&x2);
+    uint4 y1, y2;
+    uint32_t* w1 = reinterpret_cast<uint32_t*>(&y1);
+    uint32_t* w2 = reinterpret_cast<uint32_t*>(&y2);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f1 = unpack2<BF16>(u1[e]);
+      const float2 f2 = unpack2<BF16>(u2[e]);
+      const float c0 = cc[2 * e], c1 = cc[2 * e + 1];
+      const float s0 = ss[2 * e], s1 = ss[2 * e + 1];
+      // rot1 = x1*c - x2*s ; rot2 = x1*s + x2*c  (rope_apply_ref.py:49-53)
+      w1[e] = pack2<BF16>(__fsub_rn(__fmul_rn(f1.x, c0), __fmul_rn(f2.x, s0)),
+                          __fsub_rn(__fmul_rn(f1.y, c1), __fmul_rn(f2.y, s1)));
+      w2[e] = pack2<BF16>(__fadd_rn(__fmul_rn(f1.x, s0), __fmul_rn(f2.x, c0)),
+                          __fadd_rn(__fmul_rn(f1.y, s1), __fmul_rn(f2.y, c1)));
+    }
+    *reinterpret_cast<uint4*>(a_lo) = y1;
+    *reinterpret_cast<uint4*>(a_hi) = y2;
+  }
+}
+
+template <int D, bool BF16>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
@@ -70,9 +122,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + C::Q_BYTES;
-  uint8_t* sV = sK + C::STAGES * C::KV_BYTES;
+  uint8_t* sQ = smem;                          // [2][KCH][128][128B]
+  uint8_t* sK = sQ + 2 * C::Q_BYTES;           // [STAGES][KCH][128][128B]
+  uint8_t* sV = sK + C::STAGES * C::KV_BYTES;  // [STAGES][KCH][128][128B]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* bar_q_full = bars + 0;
   uint64_t* bar_q_ready = bars + 1;
@@ -80,45 +132,49 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* bar_k_empty = bar_k_full + C::STAGES;
   uint64_t* bar_v_full = bar_k_empty + C::STAGES;
   uint64_t* bar_v_empty = bar_v_full + C::STAGES;
-  uint64_t* bar_s_full = bar_v_empty + C::STAGES;  // [2]
-  uint64_t* bar_s_free = bar_s_full + 2;           // [2]
-  uint64_t* bar_p_full = bar_s_free + 2;           // [2]
-  uint64_t* bar_o_done = bar_p_full + 2;           // [1]
-  uint64_t* bar_drain = bar_o_done + 1;            // [1] abort path only
+  uint64_t* bar_s_full = bar_v_empty + C::STAGES;  // [2] per tile
+  uint64_t* bar_p_full = bar_s_full + 2;           // [2] per tile
+  uint64_t* bar_o_final = bar_p_full + 2;          // [2] per tile
+  uint64_t* bar_drain = bar_o_final + 2;           // [1] abort path only
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // heaviest query tiles first when causal
+  // heaviest tile pairs first when causal
   const int bh_count = p.B * p.Hq;
-  const int qt_lin = blockIdx.x / bh_count;
-  const int qt = p.causal ? (p.n_qtiles - 1 - qt_lin) : qt_lin;
+  const int pair_lin = blockIdx.x / bh_count;
+  const int pr = p.causal ? (p.n_pairs - 1 - pair_lin) : pair_lin;
   const int bh = blockIdx.x % bh_count;
   const int b = bh / p.Hq;
   const int h = bh % p.Hq;
   const int kvh = h / p.G;
-  const int m0 = qt * kBM;
-  int n_end = p.causal ? min(p.N, p.N - p.M + m0 + kBM) : p.N;
-  if (n_end < 0) n_end = 0;
-  const int n_kv = (n_end + kBN - 1) / kBN;
+  const int m0 = pr * 2 * kBM;
+  int n_kv[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int mt0 = m0 + t * kBM;
+    int n_end = p.causal ? min(p.N, p.N - p.M + mt0 + kBM) : p.N;
+    if (n_end < 0) n_end = 0;
+    n_kv[t] = (mt0 < p.M) ? (n_end + kBN - 1) / kBN : 0;
+  }
+  const int n_kv_max = max(n_kv[0], n_kv[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 1);
-    mbar_init(bar_q_ready, 128);
+    mbar_init(bar_q_ready, 256);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar_k_full + s, 1);
       mbar_init(bar_k_empty + s, 1);
       mbar_init(bar_v_full + s, 1);
       mbar_init(bar_v_empty + s, 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar_s_full + s, 1);
-      mbar_init(bar_s_free + s, 128);
-      mbar_init(bar_p_full + s, 128);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar_s_full + t, 1);
+      mbar_init(bar_p_full + t, 128);
+      mbar_init(bar_o_final + t, 1);
     }
-    mbar_init(bar_o_done, 1);
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -132,18 +188,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp < 4) {
+   reg_dealloc<kRegsCtrl>();
+   if (warp == 0) {
     // ------------------------------------------------ TMA producer
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0 && n_kv_max > 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(bar_q_full, C::Q_BYTES);
+      mbar_arrive_expect_tx(bar_q_full, 2 * C::Q_BYTES);
 #pragma unroll
-      for (int c = 0; c < C::KCH; ++c)
-        tma_load_4d(sQ + c * kBM * 128, &tm_q, bar_q_full, c * 64, m0, h, b);
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(sQ + t * C::Q_BYTES + c * kBM * 128, &tm_q, bar_q_full, c * 64,
+                      m0 + t * kBM, h, b);
       int issued_k = 0, issued_v = 0;
-      for (int j = 0; j < n_kv; ++j) {
+      for (int j = 0; j < n_kv_max; ++j) {
         const int st = j % C::STAGES;
         const uint32_t ph = (j / C::STAGES) & 1;
         if (!mbar_wait_bounded(bar_k_empty + st, ph ^ 1, abort_flag, kWaitLimitNs)) break;
@@ -173,75 +234,115 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0 && n_kv_max > 0) {
       constexpr int fmt = BF16 ? 1 : 0;
       constexpr uint32_t idesc_s = umma_idesc_f16(kBM, kBN, fmt, 0, 0);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBM, D, fmt, 0, 1);
       const uint32_t q_base = smem_u32(sQ);
       const uint32_t k_base = smem_u32(sK);
       const uint32_t v_base = smem_u32(sV);
-      bool ok = mbar_wait_bounded(bar_q_ready, 0, abort_flag, kWaitLimitNs);
-      tc_fence_after();
-
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
-        const int s = i & 1;
-        const uint32_t sp = (i >> 1) & 1;
-        if (!mbar_wait_bounded(bar_p_full + s, sp, abort_flag, kWaitLimitNs)) return false;
-        if (!mbar_wait_bounded(bar_v_full + st, ph, abort_flag, kWaitLimitNs)) return false;
-        tc_fence_after();
-        const uint32_t p_col = s ? C::TM_P1 : C::TM_P0;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bdesc = umma_smem_desc(v_base + st * C::KV_BYTES + kk * 16 * 128,
-                                                kBN * 128, 1024);
-          umma_ts(tmem + C::TM_O, tmem + p_col + kk * 8, bdesc, idesc_o,
-                  (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(bar_o_done);
-        umma_commit(bar_v_empty + st);
-        return true;
-      };
-
-      for (int j = 0; ok && j < n_kv; ++j) {
+      auto issue_s = [&](int t, int j) {
         const int st = j % C::STAGES;
-        const uint32_t ph = (j / C::STAGES) & 1;
-        const int s = j & 1;
-        const uint32_t sp = (j >> 1) & 1;
-        if (!mbar_wait_bounded(bar_k_full + st, ph, abort_flag, kWaitLimitNs)) { ok = false; break; }
-        if (!mbar_wait_bounded(bar_s_free + s, sp ^ 1, abort_flag, kWaitLimitNs)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t s_col = s ? C::TM_S1 : C::TM_S0;
+        const uint32_t s_col = t ? C::TM_S1 : C::TM_S0;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int c = kk >> 2;
           const uint32_t off = (kk & 3) * 32;
-          const uint64_t adesc = umma_smem_desc(q_base + c * kBM * 128 + off, 16, 1024);
+          const uint64_t adesc =
+              umma_smem_desc(q_base + t * C::Q_BYTES + c * kBM * 128 + off, 16, 1024);
           const uint64_t bdesc =
               umma_smem_desc(k_base + st * C::KV_BYTES + c * kBN * 128 + off, 16, 1024);
           umma_ss(tmem + s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(bar_s_full + s);
-        umma_commit(bar_k_empty + st);
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+        umma_commit(bar_s_full + t);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const int st = j % C::STAGES;
+        const uint32_t p_col = t ? C::TM_S1 : C::TM_S0;
+        const uint32_t o_col = t ? C::TM_O1 : C::TM_O0;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bdesc = umma_smem_desc(v_base + st * C::KV_BYTES + kk * 16 * 128,
+                                                kBN * 128, 1024);
+          umma_ts(tmem + o_col, tmem + p_col + kk * 8, bdesc, idesc_o,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (j == n_kv[t] - 1) umma_commit(bar_o_final + t);
+      };
+
+      bool ok = mbar_wait_bounded(bar_q_ready, 0, abort_flag, kWaitLimitNs) &&
+                mbar_wait_bounded(bar_k_full, 0, abort_flag, kWaitLimitNs);
+      if (ok) {
+        tc_fence_after();
+        if (n_kv[0] > 0) issue_s(0, 0);
+        if (n_kv[1] > 0) issue_s(1, 0);
+        umma_commit(bar_k_empty);
       }
-      if (ok) ok = issue_pv(n_kv - 1);
+      for (int j = 0; ok && j < n_kv_max; ++j) {
+        const int st = j % C::STAGES;
+        const uint32_t ph = (j / C::STAGES) & 1;
+        const int jn = j + 1;
+        const int stn = jn % C::STAGES;
+        const uint32_t phn = (jn / C::STAGES) & 1;
+        if (!(ok = mbar_wait_bounded(bar_v_full + st, ph, abort_flag, kWaitLimitNs))) break;
+        if (j < n_kv[0]) {
+          if (!(ok = mbar_wait_bounded(bar_p_full + 0, j & 1, abort_flag, kWaitLimitNs))) break;
+          tc_fence_after();
+          issue_pv(0, j);
+        }
+        if (jn < n_kv_max) {
+          if (!(ok = mbar_wait_bounded(bar_k_full + stn, phn, abort_flag, kWaitLimitNs))) break;
+          tc_fence_after();
+          if (jn < n_kv[0]) issue_s(0, jn);
+        }
+        if (j < n_kv[1]) {
+          if (!(ok = mbar_wait_bounded(bar_p_full + 1, j & 1, abort_flag, kWaitLimitNs))) break;
+          tc_fence_after();
+          issue_pv(1, j);
+        }
+        umma_commit(bar_v_empty + st);
+        if (jn < n_kv_max) {
+          if (jn < n_kv[1]) issue_s(1, jn);
+          umma_commit(bar_k_empty + stn);
+        }
+      }
       if (!ok) {
         raise_status(CIE_DEV_TIMEOUT);
         umma_commit(bar_drain);  // all MMAs issued so far must finish before TMEM is freed
         mbar_wait_timeout(bar_drain, 0, kWaitLimitNs);
       }
     }
+   }
   } else {
-    // ------------------------------------------------ softmax warpgroup
-    const int wq = warp & 3;            // TMEM lane quarter this warp may access
-    const int row = wq * 32 + lane;     // query row within the tile == TMEM lane
+    reg_alloc<kRegsSoftmax>();
+    // ------------------------------------------------ softmax warpgroups
+    const int t = (warp - 4) >> 2;       // query tile of this warpgroup
+    const int wq = warp & 3;             // TMEM lane quarter this warp may access
+    const int row = wq * 32 + lane;      // query row within the tile == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
-    const int gm = m0 + row;            // global query index
+    const int gm = m0 + t * kBM + row;   // global query index
+    const int nkv = n_kv[t];
+    const uint32_t s_col = t ? C::TM_S1 : C::TM_S0;
+    const uint32_t o_col = t ? C::TM_O1 : C::TM_O0;
     using elem_t = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    bool ok = true;
 
-    if (n_kv == 0) {
+    if (n_kv_max > 0) {
+      ok = mbar_wait_bounded(bar_q_full, 0, abort_flag, kWaitLimitNs);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok && p.cos != nullptr && gm < p.M) {
+        int pos = p.rope_q_pos0 + gm;
+        if (pos < 0 || pos >= p.rope_max_pos) {
+          raise_status(CIE_DEV_BAD_POSITION);
+          pos = pos < 0 ? 0 : p.rope_max_pos - 1;
+        }
+        rope_q_row<D, BF16>(sQ + t * C::Q_BYTES, row, pos, p.cos, p.sin);
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(bar_q_ready);
+    }
+
+    if (nkv == 0) {
       // no visible keys: N == 0 -> zeros (matches the fp32 reference), else NaN rows
       if (gm < p.M) {
         elem_t* o = reinterpret_cast<elem_t*>(p.o) + b * p.o_sb + h * p.o_sh + gm * p.o_sm;
@@ -251,75 +352,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           else o[d] = __float2half_rn(fill);
         }
       }
-    } else {
-      bool ok = mbar_wait_bounded(bar_q_full, 0, abort_flag, kWaitLimitNs);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok && p.cos != nullptr && gm < p.M) {
-        // rotate this thread's Q row in shared memory (half-split RoPE)
-        int pos = p.rope_q_pos0 + gm;
-        if (pos < 0 || pos >= p.rope_max_pos) {
-          raise_status(CIE_DEV_BAD_POSITION);
-          pos = pos < 0 ? 0 : p.rope_max_pos - 1;
-        }
-        constexpr int HALF = D / 2;
-        const float* cr = p.cos + static_cast<int64_t>(pos) * HALF;
-        const float* sr = p.sin + static_cast<int64_t>(pos) * HALF;
-#pragma unroll
-        for (int pc = 0; pc < HALF / 8; ++pc) {
-          const int e_lo = pc * 8, e_hi = HALF + pc * 8;
-          uint8_t* a_lo = sQ + (e_lo / 64) * kBM * 128 + row * 128 +
-                          ((((e_lo % 64) / 8) ^ (row & 7)) * 16);
-          uint8_t* a_hi = sQ + (e_hi / 64) * kBM * 128 + row * 128 +
-                          ((((e_hi % 64) / 8) ^ (row & 7)) * 16);
-          uint4 x1 = *reinterpret_cast<uint4*>(a_lo);
-          uint4 x2 = *reinterpret_cast<uint4*>(a_hi);
-          const uint32_t* u1 = reinterpret_cast<const uint32_t*>(&x1);
-          const uint32_t* u2 = reinterpret_cast<const uint32_t*>(&x2);
-          uint4 y1, y2;
-          uint32_t* w1 = reinterpret_cast<uint32_t*>(&y1);
-          uint32_t* w2 = reinterpret_cast<uint32_t*>(&y2);
-          const float4 ca = *reinterpret_cast<const float4*>(cr + e_lo);
-          const float4 cb = *reinterpret_cast<const float4*>(cr + e_lo + 4);
-          const float4 sa = *reinterpret_cast<const float4*>(sr + e_lo);
-          const float4 sb = *reinterpret_cast<const float4*>(sr + e_lo + 4);
-          const float cc[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
-          const float ss[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f1 = unpack2<BF16>(u1[e]);
-            const float2 f2 = unpack2<BF16>(u2[e]);
-            const float c0 = cc[2 * e], c1 = cc[2 * e + 1];
-            const float s0 = ss[2 * e], s1 = ss[2 * e + 1];
-            w1[e] = pack2<BF16>(__fsub_rn(__fmul_rn(f1.x, c0), __fmul_rn(f2.x, s0)),
-                                __fsub_rn(__fmul_rn(f1.y, c1), __fmul_rn(f2.y, s1)));
-            w2[e] = pack2<BF16>(__fadd_rn(__fmul_rn(f1.x, s0), __fmul_rn(f2.x, c0)),
-                                __fadd_rn(__fmul_rn(f1.y, s1), __fmul_rn(f2.y, c1)));
-          }
-          *reinterpret_cast<uint4*>(a_lo) = y1;
-          *reinterpret_cast<uint4*>(a_hi) = y2;
-        }
-        fence_proxy_async_smem();
-      }
-      mbar_arrive(bar_q_ready);
-
+    } else if (ok) {
       const int lim = p.causal ? (p.N - p.M + gm) : (p.N - 1);  // keys <= lim are visible
       float m_run = -INFINITY;  // running max, log2 domain, scaled
       float l_run = 0.f;
       float sv[kBN];
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int s = j & 1;
-        const uint32_t sp = (j >> 1) & 1;
-        ok = mbar_wait_bounded(bar_s_full + s, sp, abort_flag, kWaitLimitNs);
+      for (int j = 0; ok && j < nkv; ++j) {
+        ok = mbar_wait_bounded(bar_s_full + t, j & 1, abort_flag, kWaitLimitNs);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t s_col = s ? C::TM_S1 : C::TM_S0;
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c)
           tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
         tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(bar_s_free + s);
 
         const int n0 = j * kBN;
         if (n0 + kBN - 1 > lim) {
@@ -327,41 +373,38 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           for (int c = 0; c < kBN; ++c)
             if (n0 + c > lim) sv[c] = -INFINITY;
         }
-        float mx = sv[0];
+        float mx0 = fmaxf(sv[0], sv[1]), mx1 = fmaxf(sv[2], sv[3]);
 #pragma unroll
-        for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
-        const float m_new = fmaxf(m_run, mx * p.scale_log2);
-
-        if (j > 0) {
-          ok = mbar_wait_bounded(bar_o_done, (j - 1) & 1, abort_flag, kWaitLimitNs);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc_fence_after();
+        for (int c = 4; c < kBN; c += 4) {
+          mx0 = fmaxf(mx0, fmaxf(sv[c], sv[c + 1]));
+          mx1 = fmaxf(mx1, fmaxf(sv[c + 2], sv[c + 3]));
+        }
+        const float m_new = fmaxf(m_run, fmaxf(mx0, mx1) * p.scale_log2);
+        if (j == 0) {
+          m_run = m_new;  // PV of tile 0 starts O from zero
+        } else {
+          // S_t_j complete implies PV_t_{j-1} complete: O_t may be rescaled now
           const bool need = m_new > m_run + 8.0f;
           if (__any_sync(0xffffffffu, need)) {
             const float alpha = need ? ex2(m_run - m_new) : 1.0f;
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-              uint32_t ov[32];
-              tmem_ld32(tmem + lane_addr + C::TM_O + c * 32, ov);
+            for (int c = 0; c < D / 16; ++c) {
+              uint32_t ov[16];
+              tmem_ld16(tmem + lane_addr + o_col + c * 16, ov);
               tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 32; ++e)
+              for (int e = 0; e < 16; ++e)
                 ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-              tmem_st32(tmem + lane_addr + C::TM_O + c * 32, ov);
+              tmem_st16(tmem + lane_addr + o_col + c * 16, ov);
             }
-            tmem_wait_st();
             if (need) {
               l_run *= alpha;
               m_run = m_new;
             }
           }
-        } else {
-          m_run = m_new;
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        const uint32_t p_col = s ? C::TM_P1 : C::TM_P0;
-        float lsum = 0.f;
+        float lsum0 = 0.f, lsum1 = 0.f;
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
           uint32_t pk[32];
@@ -369,19 +412,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           for (int c = 0; c < 64; c += 2) {
             const float p0 = ex2(fmaf(sv[hb * 64 + c], p.scale_log2, -m_use));
             const float p1 = ex2(fmaf(sv[hb * 64 + c + 1], p.scale_log2, -m_use));
-            lsum += p0 + p1;
+            lsum0 += p0;
+            lsum1 += p1;
             pk[c / 2] = pack2<BF16>(p0, p1);
           }
-          tmem_st32(tmem + lane_addr + p_col + hb * 32, pk);
+          tmem_st32(tmem + lane_addr + s_col + hb * 32, pk);
         }
-        l_run += lsum;
+        l_run += lsum0 + lsum1;
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar_p_full + s);
+        mbar_arrive(bar_p_full + t);
       }
 
       if (ok) {
-        ok = mbar_wait_bounded(bar_o_done, (n_kv - 1) & 1, abort_flag, kWaitLimitNs);
+        ok = mbar_wait_bounded(bar_o_final + t, 0, abort_flag, kWaitLimitNs);
         ok = __all_sync(0xffffffffu, ok);
       }
       if (ok) {
@@ -391,7 +435,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t ov[32];
-          tmem_ld32(tmem + lane_addr + C::TM_O + c * 32, ov);
+          tmem_ld32(tmem + lane_addr + o_col + c * 32, ov);
           tmem_wait_ld();
           if (gm < p.M) {
             uint32_t pk[16];
@@ -405,10 +449,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
           }
         }
-      } else {
-        raise_status(CIE_DEV_TIMEOUT);
       }
     }
+    if (!ok) raise_status(CIE_DEV_TIMEOUT);
   }
 
   tc_fence_before();
@@ -450,7 +493,7 @@ static int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CU
   constexpr int smem = PfCfg<D>::SMEM;
   auto kern = prefill_attn_kernel<D, BF16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  const int grid = prm.n_qtiles * prm.B * prm.Hq;
+  const int grid = prm.n_pairs * prm.B * prm.Hq;
   kern<<<grid, kPfThreads, smem, st>>>(mq, mk, mv, prm);
   CIE_CHECK_LAUNCH("prefill_attn_kernel");
   return CIE_OK;
@@ -572,7 +615,7 @@ extern "C" int cie_prefill_attn(const void* q, const void* k, const void* v, voi
   prm.M = M;
   prm.N = N;
   prm.G = Hq / Hkv;
-  prm.n_qtiles = (M + kBM - 1) / kBM;
+  prm.n_pairs = (M + 2 * kBM - 1) / (2 * kBM);
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
   prm.o = o;
