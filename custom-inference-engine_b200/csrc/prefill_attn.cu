@@ -41,6 +41,19 @@ constexpr int kPfThreads = 384;  // 3 warpgroups
 // (producer, MMA issuer, 2 idle warps) gives registers to the two softmax
 // warpgroups: 48 + 224 + 224 = 496 <= 3 * 168 per scheduler.
 constexpr int kRegsCtrl = 48;
+// Optional: every kEmuEvery-th pair of probabilities is exponentiated on the FMA
+// pipe (exp2_poly2) instead of the MUFU unit. Off by default: measured on B200
+// the softmax is issue-bound rather than MUFU-bound (every 4th pair: 1058 ->
+// 844 TFLOP/s at d = 128), so the extra FMA-pipe instructions cost more than the
+// MUFU cycles they free. Build with -DCIE_EMU_EVERY_D128=N / _D64=N to enable.
+#ifndef CIE_EMU_EVERY_D128
+#define CIE_EMU_EVERY_D128 0
+#endif
+#ifndef CIE_EMU_EVERY_D64
+#define CIE_EMU_EVERY_D64 0
+#endif
+template <int D>
+constexpr int kEmuEvery = D >= 128 ? CIE_EMU_EVERY_D128 : CIE_EMU_EVERY_D64;
 constexpr int kRegsSoftmax = 224;
 constexpr int kBM = 128;         // rows of one query tile; a CTA owns two
 constexpr int kBN = 128;         // keys per K/V tile
@@ -368,7 +381,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tmem_wait_ld();
 
         const int n0 = j * kBN;
-        if (n0 + kBN - 1 > lim) {
+        // a tile that reaches past some row's last visible key takes the masked path
+        const bool masked = __any_sync(0xffffffffu, n0 + kBN - 1 > lim);
+        if (masked) {
 #pragma unroll
           for (int c = 0; c < kBN; ++c)
             if (n0 + c > lim) sv[c] = -INFINITY;
@@ -376,12 +391,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         float mx0 = fmaxf(sv[0], sv[1]), mx1 = fmaxf(sv[2], sv[3]);
 #pragma unroll
         for (int c = 4; c < kBN; c += 4) {
-          mx0 = fmaxf(mx0, fmaxf(sv[c], sv[c + 1]));
-          mx1 = fmaxf(mx1, fmaxf(sv[c + 2], sv[c + 3]));
+          mx0 = fmax3(mx0, sv[c], sv[c + 1]);
+          mx1 = fmax3(mx1, sv[c + 2], sv[c + 3]);
         }
         const float m_new = fmaxf(m_run, fmaxf(mx0, mx1) * p.scale_log2);
         if (j == 0) {
-          m_run = m_new;  // PV of tile 0 starts O from zero
+          m_run = m_new;  // PV of tile t starts O from zero
         } else {
           // S_t_j complete implies PV_t_{j-1} complete: O_t may be rescaled now
           const bool need = m_new > m_run + 8.0f;
@@ -404,20 +419,34 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           }
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        float lsum0 = 0.f, lsum1 = 0.f;
+        // p = 2^(s * scale - m): packed FFMA, then MUFU ex2 for most pairs and
+        // the FMA-pipe polynomial for every kEmuEvery-th pair of unmasked tiles
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t nm2 = f2_pack(-m_use, -m_use);
+        uint64_t sum2 = f2_pack(0.f, 0.f);
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
           uint32_t pk[32];
 #pragma unroll
           for (int c = 0; c < 64; c += 2) {
-            const float p0 = ex2(fmaf(sv[hb * 64 + c], p.scale_log2, -m_use));
-            const float p1 = ex2(fmaf(sv[hb * 64 + c + 1], p.scale_log2, -m_use));
-            lsum0 += p0;
-            lsum1 += p1;
-            pk[c / 2] = pack2<BF16>(p0, p1);
+            const uint64_t x2 = ffma2(f2_pack(sv[hb * 64 + c], sv[hb * 64 + c + 1]), sc2, nm2);
+            uint64_t p2;
+            if (kEmuEvery<D> > 0 && !masked && ((c / 2) % kEmuEvery<D>) == kEmuEvery<D> - 1) {
+              p2 = exp2_poly2(x2);
+            } else {
+              float a, b2;
+              f2_unpack(x2, a, b2);
+              p2 = f2_pack(ex2(a), ex2(b2));
+            }
+            sum2 = fadd2(sum2, p2);
+            float pa, pb;
+            f2_unpack(p2, pa, pb);
+            pk[c / 2] = pack2<BF16>(pa, pb);
           }
           tmem_st32(tmem + lane_addr + s_col + hb * 32, pk);
         }
+        float lsum0, lsum1;
+        f2_unpack(sum2, lsum0, lsum1);
         l_run += lsum0 + lsum1;
         tmem_wait_st();
         tc_fence_before();

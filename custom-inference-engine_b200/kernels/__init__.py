@@ -27,21 +27,9 @@ def require_extension() -> None:
         raise RuntimeError(str(e)) from e
 
 
-from kernels.flash_attention import (  # noqa: E402
-    apply_rotary,
-    flash_attention,
-    gather_kv,
-    paged_attention,
-    rope_append,
-)
+# The entry points live in kernels.flash_attention, as in the reference
+# (``from kernels.flash_attention import flash_attention``); the package does not
+# re-export them so that ``kernels.flash_attention`` stays the module.
 from kernels.rope import build_rope_cache  # noqa: E402
 
-__all__ = [
-    "require_extension",
-    "flash_attention",
-    "paged_attention",
-    "gather_kv",
-    "rope_append",
-    "apply_rotary",
-    "build_rope_cache",
-]
+__all__ = ["require_extension", "build_rope_cache"]
