@@ -55,11 +55,15 @@ def gather_output(local_out: torch.Tensor, group=None, async_op: bool = False):
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
-    out = torch.empty((world, *local_out.shape), dtype=local_out.dtype, device=local_out.device)
+    # rank-major concatenation along dim 0 (the layout every backend accepts)
+    flat = torch.empty((world * local_out.shape[0], *local_out.shape[1:]), dtype=local_out.dtype,
+                       device=local_out.device)
+    out = flat.view(world, *local_out.shape)
     if world == 1:
         out[0].copy_(local_out)
         return (out, None) if async_op else out
-    work = dist.all_gather_into_tensor(out, local_out.contiguous(), group=group, async_op=async_op)
+    work = dist.all_gather_into_tensor(flat, local_out.contiguous(), group=group,
+                                       async_op=async_op)
     return (out, work) if async_op else out
 
 
