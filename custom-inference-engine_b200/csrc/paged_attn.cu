@@ -73,7 +73,7 @@ struct PagedCfg {
   static constexpr int ROWB = (D * 2 < 128) ? D * 2 : 128;  // bytes per swizzled sub-row
   static constexpr int KCS = ROWB / 16;                     // 16B chunks per sub-row
   static constexpr int SUBS = (D * 2) / ROWB;               // 64-column slices per row
-  static constexpr int kStages = (D <= 64) ? 4 : (D == 128 ? 3 : 2);
+  static constexpr int kStages = (D <= 64) ? 3 : (D == 128 ? 3 : 2);
   static constexpr int kTileBytes = kTileTok * D * 2;  // K or V tile
   static constexpr int kStageBytes = 2 * kTileBytes;   // K + V
   static constexpr int kWarpBytes = kStages * kStageBytes;
@@ -102,7 +102,7 @@ template <int D, int MT>
 __host__ __device__ constexpr int paged_pipe_or_merge() {
   constexpr int RG = 16 * MT;
   constexpr int pipe = PagedCfg<D>::kPipeBytes;
-  constexpr int merge = kPagedWarps * RG * (D + 2) * 4;
+  constexpr int merge = kPagedWarps * RG * (D + 6) * 4;
   return pipe > merge ? pipe : merge;
 }
 
@@ -169,58 +169,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
     }
   }
 
-  // ---- rotated Q tile -> shared memory (16B-chunk swizzle) ----
-  {
-    using elem_t = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    const elem_t* q = reinterpret_cast<const elem_t*>(p.q);
-    constexpr int HALF = D / 2;
-    constexpr int PAIR_CHUNKS = HALF / 8;  // 8 rotation pairs per work item
-    for (int w = tid; w < RG * PAIR_CHUNKS; w += blockDim.x) {
-      const int r = w / PAIR_CHUNKS;
-      const int pc = w % PAIR_CHUNKS;
-      const int gr = row0 + r;
-      uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-      if (gr < R) {
-        const int gh = gr / p.M, m = gr % p.M;
-        const int h = kvh * p.G + gh;
-        const elem_t* src = q + b * p.q_sb + h * p.q_sh + m * p.q_sm;
-        const uint4 x1 = *reinterpret_cast<const uint4*>(src + pc * 8);
-        const uint4 x2 = *reinterpret_cast<const uint4*>(src + HALF + pc * 8);
-        if (p.cos != nullptr) {
-          int pos = q_pos_base + m;
-          if (pos < 0 || pos >= p.rope_max_pos) {
-            raise_status(CIE_DEV_BAD_POSITION);
-            pos = pos < 0 ? 0 : p.rope_max_pos - 1;
-          }
-          const float* cr = p.cos + static_cast<int64_t>(pos) * HALF + pc * 8;
-          const float* sr = p.sin + static_cast<int64_t>(pos) * HALF + pc * 8;
-          const uint32_t* a = reinterpret_cast<const uint32_t*>(&x1);
-          const uint32_t* c = reinterpret_cast<const uint32_t*>(&x2);
-          uint32_t* lo_w = reinterpret_cast<uint32_t*>(&lo);
-          uint32_t* hi_w = reinterpret_cast<uint32_t*>(&hi);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 u1 = unpack2<BF16>(a[e]);
-            const float2 u2 = unpack2<BF16>(c[e]);
-            const float c0 = cr[2 * e], c1 = cr[2 * e + 1];
-            const float s0 = sr[2 * e], s1 = sr[2 * e + 1];
-            // rot1 = x1*c - x2*s ; rot2 = x1*s + x2*c  (rope_apply_ref.py:49-53)
-            lo_w[e] = pack2<BF16>(__fsub_rn(__fmul_rn(u1.x, c0), __fmul_rn(u2.x, s0)),
-                                  __fsub_rn(__fmul_rn(u1.y, c1), __fmul_rn(u2.y, s1)));
-            hi_w[e] = pack2<BF16>(__fadd_rn(__fmul_rn(u1.x, s0), __fmul_rn(u2.x, c0)),
-                                  __fadd_rn(__fmul_rn(u1.y, s1), __fmul_rn(u2.y, c1)));
-          }
-        } else {
-          lo = x1;
-          hi = x2;
-        }
-      }
-      const int c_lo = pc, c_hi = HALF / 8 + pc;
-      *reinterpret_cast<uint4*>(qs + r * (D * 2) + swz<KC>(r, c_lo) * 16) = lo;
-      *reinterpret_cast<uint4*>(qs + r * (D * 2) + swz<KC>(r, c_hi) * 16) = hi;
-    }
-  }
-  __syncthreads();
+  __syncthreads();  // barrier init visible before the first TMA is issued
 
   // ---- per-warp streaming of K/V tiles ----
   const int g = lane >> 2;  // row within an 8-row group
@@ -325,6 +274,71 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
     }
   };
 
+  // K/V prologue first: the copies are in flight while Q is rotated below
+  const int my_tiles = n_tiles > warp ? (n_tiles - warp + kPagedWarps - 1) / kPagedWarps : 0;
+  int issued = 0;
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; ++s) {
+    if (s < my_tiles) {
+      issue_tile(warp + kPagedWarps * s, s);
+      ++issued;
+    }
+    if constexpr (!TMA) cp_async_commit();
+  }
+
+  // ---- rotated Q tile -> shared memory (16B-chunk swizzle) ----
+  {
+    using elem_t = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    const elem_t* q = reinterpret_cast<const elem_t*>(p.q);
+    constexpr int HALF = D / 2;
+    constexpr int PAIR_CHUNKS = HALF / 8;  // 8 rotation pairs per work item
+    for (int w = tid; w < RG * PAIR_CHUNKS; w += blockDim.x) {
+      const int r = w / PAIR_CHUNKS;
+      const int pc = w % PAIR_CHUNKS;
+      const int gr = row0 + r;
+      uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+      if (gr < R) {
+        const int gh = gr / p.M, m = gr % p.M;
+        const int h = kvh * p.G + gh;
+        const elem_t* src = q + b * p.q_sb + h * p.q_sh + m * p.q_sm;
+        const uint4 x1 = *reinterpret_cast<const uint4*>(src + pc * 8);
+        const uint4 x2 = *reinterpret_cast<const uint4*>(src + HALF + pc * 8);
+        if (p.cos != nullptr) {
+          int pos = q_pos_base + m;
+          if (pos < 0 || pos >= p.rope_max_pos) {
+            raise_status(CIE_DEV_BAD_POSITION);
+            pos = pos < 0 ? 0 : p.rope_max_pos - 1;
+          }
+          const float* cr = p.cos + static_cast<int64_t>(pos) * HALF + pc * 8;
+          const float* sr = p.sin + static_cast<int64_t>(pos) * HALF + pc * 8;
+          const uint32_t* a = reinterpret_cast<const uint32_t*>(&x1);
+          const uint32_t* c = reinterpret_cast<const uint32_t*>(&x2);
+          uint32_t* lo_w = reinterpret_cast<uint32_t*>(&lo);
+          uint32_t* hi_w = reinterpret_cast<uint32_t*>(&hi);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 u1 = unpack2<BF16>(a[e]);
+            const float2 u2 = unpack2<BF16>(c[e]);
+            const float c0 = cr[2 * e], c1 = cr[2 * e + 1];
+            const float s0 = sr[2 * e], s1 = sr[2 * e + 1];
+            // rot1 = x1*c - x2*s ; rot2 = x1*s + x2*c  (rope_apply_ref.py:49-53)
+            lo_w[e] = pack2<BF16>(__fsub_rn(__fmul_rn(u1.x, c0), __fmul_rn(u2.x, s0)),
+                                  __fsub_rn(__fmul_rn(u1.y, c1), __fmul_rn(u2.y, s1)));
+            hi_w[e] = pack2<BF16>(__fadd_rn(__fmul_rn(u1.x, s0), __fmul_rn(u2.x, c0)),
+                                  __fadd_rn(__fmul_rn(u1.y, s1), __fmul_rn(u2.y, c1)));
+          }
+        } else {
+          lo = x1;
+          hi = x2;
+        }
+      }
+      const int c_lo = pc, c_hi = HALF / 8 + pc;
+      *reinterpret_cast<uint4*>(qs + r * (D * 2) + swz<KC>(r, c_lo) * 16) = lo;
+      *reinterpret_cast<uint4*>(qs + r * (D * 2) + swz<KC>(r, c_hi) * 16) = hi;
+    }
+  }
+  __syncthreads();
+
   // Q A-fragments (held in registers when small).
   constexpr bool kQReg = (MT * D) <= 128;
   uint32_t qa[kQReg ? MT : 1][kQReg ? D / 16 : 1][4];
@@ -351,17 +365,6 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
       lim[mt][hf] = p.causal ? (kv_len - p.M + m) : (kv_len - 1);
     }
   const int lim_min = p.causal ? (kv_len - p.M) : (kv_len - 1);
-
-  const int my_tiles = n_tiles > warp ? (n_tiles - warp + kPagedWarps - 1) / kPagedWarps : 0;
-  int issued = 0;
-#pragma unroll
-  for (int s = 0; s < STAGES - 1; ++s) {
-    if (s < my_tiles) {
-      issue_tile(warp + kPagedWarps * s, s);
-      ++issued;
-    }
-    if constexpr (!TMA) cp_async_commit();
-  }
 
   for (int it = 0; it < my_tiles; ++it) {
     {
@@ -517,8 +520,9 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
   __syncthreads();  // pipeline ring is reused below
 
   // ---- merge the 4 warps in shared memory ----
-  float* sm_o = reinterpret_cast<float*>(pipe);   // [W][RG][D]
-  float* sm_m = sm_o + kPagedWarps * RG * D;      // [W][RG]
+  constexpr int OS = D + 4;                       // padded row: conflict-free float2 stores
+  float* sm_o = reinterpret_cast<float*>(pipe);   // [W][RG][OS]
+  float* sm_m = sm_o + kPagedWarps * RG * OS;     // [W][RG]
   float* sm_l = sm_m + kPagedWarps * RG;          // [W][RG]
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
@@ -535,7 +539,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
 #pragma unroll
       for (int nt = 0; nt < D / 8; ++nt) {
         float2 v2 = make_float2(o_acc[mt][nt][2 * hf], o_acc[mt][nt][2 * hf + 1]);
-        *reinterpret_cast<float2*>(sm_o + (warp * RG + r) * D + nt * 8 + 2 * t4) = v2;
+        *reinterpret_cast<float2*>(sm_o + (warp * RG + r) * OS + nt * 8 + 2 * t4) = v2;
       }
     }
   __syncthreads();
@@ -555,7 +559,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
 #pragma unroll
     for (int w = 0; w < kPagedWarps; ++w) {
       const float wt = ex2(sm_m[w * RG + r] - mu);
-      acc += wt * sm_o[(w * RG + r) * D + d];
+      acc += wt * sm_o[(w * RG + r) * OS + d];
       l += wt * sm_l[w * RG + r];
     }
     if (direct) {
