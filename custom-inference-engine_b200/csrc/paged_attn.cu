@@ -51,6 +51,7 @@ struct PagedParams {
   int rope_max_pos;
   int B, Hq, Hkv, M, G;
   int num_blocks, block_size, max_blocks;
+  int bs_log2;  // log2(block_size) when it is a power of two, else -1
   int64_t q_sb, q_sh, q_sm;
   int64_t o_sb, o_sh, o_sm;
   int split_tokens;
@@ -110,7 +111,8 @@ template <int D, int MT>
 __host__ __device__ constexpr int paged_smem_bytes() {
   // pipeline ring (reused for the cross-warp merge) + rotated Q tile + barriers
   return paged_pipe_or_merge<D, MT>() + 16 * MT * D * 2 +
-         kPagedWarps * PagedCfg<D>::kStages * 8 + 16 + 1024;
+         kPagedWarps * PagedCfg<D>::kStages * 8 + 16 + kPagedWarps * PagedCfg<D>::kStages * 4 +
+         1024;
 }
 
 template <int D, int MT, bool BF16, bool PAGED, bool TMA>
@@ -129,6 +131,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
   uint8_t* qs = smem + paged_pipe_or_merge<D, MT>();
   uint64_t* full_bars = reinterpret_cast<uint64_t*>(qs + RG * D * 2);  // [warps][STAGES]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full_bars + kPagedWarps * STAGES);
+  int* stage_bad = const_cast<int*>(abort_flag) + 4;  // [warps][STAGES]
 
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / p.row_groups;
@@ -198,7 +201,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
   // physical block of the 16-token tile starting at t0 (TMA path: one block
   // holds the whole tile); -1 when the table entry is invalid
   auto tile_block = [&](int t0) -> int {
-    const int lb = t0 / p.block_size;
+    const int lb = p.bs_log2 >= 0 ? (t0 >> p.bs_log2) : t0 / p.block_size;
     const int blk = lb < p.max_blocks ? table[lb] : -1;
     return (blk < 0 || blk >= p.num_blocks) ? -1 : blk;
   };
@@ -215,7 +218,10 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
         if constexpr (PAGED) {
           const int blk = tile_block(t0);
           ok = blk >= 0;
-          c2 = blk * p.block_size + (t0 % p.block_size);
+          c2 = blk * p.block_size +
+               (p.bs_log2 >= 0 ? (t0 & (p.block_size - 1)) : t0 % p.block_size);
+          // record a refused block id for the consumer lanes (read after the wait)
+          stage_bad[warp * STAGES + stage] = ok ? 0 : 1;
         } else {
           c2 = kvh;
           c3 = b;
@@ -390,7 +396,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
       // block id was refused is zeroed entirely
       int valid_rows = kTileTok;
       if constexpr (PAGED) {
-        if (tile_block(t0) < 0) valid_rows = 0;
+        if (stage_bad[warp * STAGES + stage]) valid_rows = 0;
         else if (t0 + kTileTok > kv_len) valid_rows = kv_len - t0;
       }
       if (valid_rows < kTileTok) {
@@ -438,7 +444,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
       }
     }
 
-    // online softmax (log2 domain); O is rescaled only when some row's max grew
+    // online softmax (log2 domain); O is rescaled only when a row's max grew by > 2^8
     const bool need_mask = (t0 + kTileTok - 1) > lim_min;
     uint32_t pa[MT][4];
     float alpha[MT][2];
@@ -462,11 +468,14 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
         float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        // keep a stale max until the row max grows by more than 2^8: O and l
+        // share it, so the result is exact and p stays <= 256
         const float m_new = fmaxf(m_run[mt][hf], mx);
-        const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        alpha[mt][hf] = ex2(m_run[mt][hf] - m_use);
-        any_rescale |= (m_new != m_run[mt][hf]);
-        m_run[mt][hf] = m_new;
+        const bool need = m_new > m_run[mt][hf] + 8.0f;
+        alpha[mt][hf] = need ? ex2(m_run[mt][hf] - m_new) : 1.0f;
+        any_rescale |= need;
+        if (need) m_run[mt][hf] = m_new;
+        const float m_use = m_run[mt][hf] == -INFINITY ? 0.f : m_run[mt][hf];
         float ps = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -940,6 +949,7 @@ extern "C" int cie_paged_attn(const void* q, const void* k_pool, const void* v_p
   prm.num_blocks = num_blocks;
   prm.block_size = block_size;
   prm.max_blocks = max_blocks;
+  prm.bs_log2 = (block_size & (block_size - 1)) == 0 ? __builtin_ctz(block_size) : -1;
   return dispatch_d<true>(prm, d, pl.mt, dtype == CIE_DTYPE_BF16,
                           reinterpret_cast<cudaStream_t>(stream));
 }
