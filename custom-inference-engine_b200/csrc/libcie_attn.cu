@@ -4,4 +4,5 @@
 #include "api.cu"
 #include "kv_ops.cu"
 #include "paged_attn.cu"
+#include "paged_noalloc.cu"
 #include "prefill_attn.cu"

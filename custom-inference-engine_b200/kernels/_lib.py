@@ -41,6 +41,8 @@ SIGNATURES: dict[str, tuple] = {
     "cie_paged_attn": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i64p,
                             _i64p, _f, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     "cie_paged_attn_workspace": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i]),
+    "cie_paged_attn_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i,
+                                    _i64p, _i64p, _f, _i, _i, _vp, _vp, _i, _i, _vp]),
     "cie_gather_kv": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "cie_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64p,
                              _i, _vp, _vp, _i, _vp]),

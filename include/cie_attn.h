@@ -6,7 +6,7 @@
  *   - All tensor pointers are CUDA device pointers owned by the caller.
  *     The library never allocates device memory; scratch space is passed in
  *     through `workspace` with a size obtained from the matching *_workspace()
- *     query.
+ *     query (cie_paged_attn_noalloc instead uses a fixed array of its own).
  *   - Work is enqueued asynchronously on `stream` (a cudaStream_t, NULL = the
  *     legacy default stream). A return value of CIE_OK means the launch was
  *     accepted; device-side faults that the kernels detect themselves (bad
@@ -117,6 +117,33 @@ int cie_paged_attn(const void* q, const void* k_pool, const void* v_pool,
 size_t cie_paged_attn_workspace(int B, int Hq, int Hkv, int M, int d,
                                 int block_size, int max_blocks,
                                 int split_tokens);
+
+/*
+ * cie_paged_attn for callers that cannot allocate device memory — hosts that
+ * own all device memory and give plugins no allocator, or serving loops that
+ * cannot afford cudaMalloc's device synchronisation between steps. It has no
+ * counterpart in the reference (the reference allocates with torch).
+ *
+ * Same arguments and results as cie_paged_attn, without workspace. Split-KV
+ * partial results go to a fixed 32 MiB scratch array inside the library's
+ * device image, held on every GPU that loads the library until the process
+ * exits. With split_tokens = 0 the partition size is grown until the
+ * partials fit; an explicit split_tokens whose partials exceed 32 MiB is
+ * rejected with CIE_ERR_WORKSPACE and a message. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture. The array is
+ * shared by all calls on a device and keeps the last call's contents (nothing
+ * in it needs to start at zero); calls that overlap on the GPU race on it and
+ * must be serialised by the caller. It never calls cudaMalloc or cudaFree.
+ */
+int cie_paged_attn_noalloc(const void* q, const void* k_pool, const void* v_pool,
+                           const int32_t* block_tables, const int32_t* kv_lens,
+                           void* o, int B, int Hq, int Hkv, int M, int d,
+                           int num_blocks, int block_size, int max_blocks,
+                           const int64_t* q_strides, const int64_t* o_strides,
+                           float scale, int causal, int dtype,
+                           const float* rope_cos, const float* rope_sin,
+                           int rope_max_pos, int split_tokens, void* stream);
 
 /*
  * Bit-exact gather of the paged history into a dense buffer:
