@@ -9,7 +9,8 @@
 //
 // One CTA owns two 128-row query tiles (Q0, Q1) of one (batch, head) and
 // streams 128-key K/V tiles through a TMA ring shared by both:
-//   warp 0      TMA producer: Q0/Q1 once, then K_j / V_j into a ring of stages
+//   warp 0      TMA producer: Q0/Q1 once, then K_j into a ring of K stages
+//   warp 2      TMA producer: V_j into a ring of V stages
 //   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
 //   warps 4..7  softmax of tile 0, warps 8..11 softmax of tile 1: thread r owns
 //               query row r == TMEM lane r (row max / sum need no shuffles),
@@ -38,14 +39,36 @@ namespace cie {
 
 constexpr int kPfThreads = 384;  // 3 warpgroups
 // Launched at 168 registers per thread (3 warps per scheduler); warpgroup 0
-// (producer, MMA issuer, 2 idle warps) gives registers to the two softmax
-// warpgroups: 48 + 224 + 224 = 496 <= 3 * 168 per scheduler.
-constexpr int kRegsCtrl = 48;
+// (producers, MMA issuer, an idle warp) gives registers to the two softmax
+// warpgroups. The split (ctrl + 2 * softmax <= 3 * 168) is the one ptxas
+// compiles without spills for each head dim.
+template <int D>
+constexpr int kRegsCtrl = D >= 128 ? 80 : 64;
+template <int D>
+constexpr int kRegsSoftmax = D >= 128 ? 208 : 216;
 // Optional: every kEmuEvery-th pair of probabilities is exponentiated on the FMA
 // pipe (exp2_poly2) instead of the MUFU unit. Off by default: measured on B200
 // the softmax is issue-bound rather than MUFU-bound (every 4th pair: 1058 ->
 // 844 TFLOP/s at d = 128), so the extra FMA-pipe instructions cost more than the
 // MUFU cycles they free. Build with -DCIE_EMU_EVERY_D128=N / _D64=N to enable.
+#ifndef CIE_KSTAGES_D128
+#define CIE_KSTAGES_D128 3
+#endif
+#ifndef CIE_VSTAGES_D128
+#define CIE_VSTAGES_D128 2
+#endif
+#ifndef CIE_KSTAGES_D64
+#define CIE_KSTAGES_D64 4
+#endif
+#ifndef CIE_VSTAGES_D64
+#define CIE_VSTAGES_D64 4
+#endif
+#ifndef CIE_MAX_CHAINS
+#define CIE_MAX_CHAINS 8
+#endif
+#ifndef CIE_SPLIT_LD
+#define CIE_SPLIT_LD 1
+#endif
 #ifndef CIE_EMU_EVERY_D128
 #define CIE_EMU_EVERY_D128 0
 #endif
@@ -54,7 +77,6 @@ constexpr int kRegsCtrl = 48;
 #endif
 template <int D>
 constexpr int kEmuEvery = D >= 128 ? CIE_EMU_EVERY_D128 : CIE_EMU_EVERY_D64;
-constexpr int kRegsSoftmax = 224;
 constexpr int kBM = 128;         // rows of one query tile; a CTA owns two
 constexpr int kBN = 128;         // keys per K/V tile
 
@@ -63,9 +85,12 @@ struct PfCfg {
   static constexpr int KCH = D / 64;  // 128-byte swizzle chunks along d
   static constexpr int Q_BYTES = kBM * D * 2;
   static constexpr int KV_BYTES = kBN * D * 2;
-  static constexpr int STAGES = (D == 64) ? 4 : 2;
-  static constexpr int BAR_OFF = 2 * Q_BYTES + 2 * STAGES * KV_BYTES;
-  static constexpr int NBARS = 2 + 4 * STAGES + 2 + 2 + 2 + 1;
+  // K and V rings are sized separately: at d = 128 three K stages and two V
+  // stages fill the 227 KB of shared memory next to the two Q tiles.
+  static constexpr int KS = (D == 64) ? CIE_KSTAGES_D64 : CIE_KSTAGES_D128;
+  static constexpr int VS = (D == 64) ? CIE_VSTAGES_D64 : CIE_VSTAGES_D128;
+  static constexpr int BAR_OFF = 2 * Q_BYTES + (KS + VS) * KV_BYTES;
+  static constexpr int NBARS = 2 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 /*tmem slot, abort*/ + 1024 /*align*/;
   static constexpr uint32_t TM_S0 = 0, TM_S1 = 128;    // P_t aliases cols [0, 64) of S_t
   static constexpr uint32_t TM_O0 = 256, TM_O1 = 256 + D;
@@ -136,16 +161,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                          // [2][KCH][128][128B]
-  uint8_t* sK = sQ + 2 * C::Q_BYTES;           // [STAGES][KCH][128][128B]
-  uint8_t* sV = sK + C::STAGES * C::KV_BYTES;  // [STAGES][KCH][128][128B]
+  uint8_t* sK = sQ + 2 * C::Q_BYTES;      // [KS][KCH][128][128B]
+  uint8_t* sV = sK + C::KS * C::KV_BYTES;  // [VS][KCH][128][128B]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* bar_q_full = bars + 0;
   uint64_t* bar_q_ready = bars + 1;
   uint64_t* bar_k_full = bars + 2;
-  uint64_t* bar_k_empty = bar_k_full + C::STAGES;
-  uint64_t* bar_v_full = bar_k_empty + C::STAGES;
-  uint64_t* bar_v_empty = bar_v_full + C::STAGES;
-  uint64_t* bar_s_full = bar_v_empty + C::STAGES;  // [2] per tile
+  uint64_t* bar_k_empty = bar_k_full + C::KS;
+  uint64_t* bar_v_full = bar_k_empty + C::KS;
+  uint64_t* bar_v_empty = bar_v_full + C::VS;
+  uint64_t* bar_s_full = bar_v_empty + C::VS;  // [2] per tile
   uint64_t* bar_p_full = bar_s_full + 2;           // [2] per tile
   uint64_t* bar_o_final = bar_p_full + 2;          // [2] per tile
   uint64_t* bar_drain = bar_o_final + 2;           // [1] abort path only
@@ -177,9 +202,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 1);
     mbar_init(bar_q_ready, 256);
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < C::KS; ++s) {
       mbar_init(bar_k_full + s, 1);
       mbar_init(bar_k_empty + s, 1);
+    }
+    for (int s = 0; s < C::VS; ++s) {
       mbar_init(bar_v_full + s, 1);
       mbar_init(bar_v_empty + s, 1);
     }
@@ -202,13 +229,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp < 4) {
-   reg_dealloc<kRegsCtrl>();
+   reg_dealloc<kRegsCtrl<D>>();
    if (warp == 0) {
-    // ------------------------------------------------ TMA producer
+    // ------------------------------------------------ TMA producer: Q and K
     if (lane == 0 && n_kv_max > 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
       mbar_arrive_expect_tx(bar_q_full, 2 * C::Q_BYTES);
 #pragma unroll
       for (int t = 0; t < 2; ++t)
@@ -216,33 +242,45 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int c = 0; c < C::KCH; ++c)
           tma_load_4d(sQ + t * C::Q_BYTES + c * kBM * 128, &tm_q, bar_q_full, c * 64,
                       m0 + t * kBM, h, b);
-      int issued_k = 0, issued_v = 0;
+      int issued = 0;
       for (int j = 0; j < n_kv_max; ++j) {
-        const int st = j % C::STAGES;
-        const uint32_t ph = (j / C::STAGES) & 1;
+        const int st = j % C::KS;
+        const uint32_t ph = (j / C::KS) & 1;
         if (!mbar_wait_bounded(bar_k_empty + st, ph ^ 1, abort_flag, kWaitLimitNs)) break;
         mbar_arrive_expect_tx(bar_k_full + st, C::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < C::KCH; ++c)
           tma_load_4d(sK + st * C::KV_BYTES + c * kBN * 128, &tm_k, bar_k_full + st, c * 64,
                       j * kBN, kvh, b);
-        issued_k = j + 1;
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        // let this CTA's copies still in flight land before its smem is released:
+        // the newest load of each stage is the latest phase of that stage's barrier
+        mbar_wait_timeout(bar_q_full, 0, kWaitLimitNs);
+        for (int j = issued - 1; j >= 0 && j >= issued - C::KS; --j)
+          mbar_wait_timeout(bar_k_full + (j % C::KS), (j / C::KS) & 1, kWaitLimitNs);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------ TMA producer: V
+    if (lane == 0 && n_kv_max > 0) {
+      tma_prefetch_desc(&tm_v);
+      int issued = 0;
+      for (int j = 0; j < n_kv_max; ++j) {
+        const int st = j % C::VS;
+        const uint32_t ph = (j / C::VS) & 1;
         if (!mbar_wait_bounded(bar_v_empty + st, ph ^ 1, abort_flag, kWaitLimitNs)) break;
         mbar_arrive_expect_tx(bar_v_full + st, C::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < C::KCH; ++c)
           tma_load_4d(sV + st * C::KV_BYTES + c * kBN * 128, &tm_v, bar_v_full + st, c * 64,
                       j * kBN, kvh, b);
-        issued_v = j + 1;
+        issued = j + 1;
       }
       if (*abort_flag) {
-        // let this CTA's copies still in flight land before its smem is released:
-        // the newest load of each stage is the latest phase of that stage's barrier
-        mbar_wait_timeout(bar_q_full, 0, kWaitLimitNs);
-        for (int j = issued_k - 1; j >= 0 && j >= issued_k - C::STAGES; --j)
-          mbar_wait_timeout(bar_k_full + (j % C::STAGES), (j / C::STAGES) & 1, kWaitLimitNs);
-        for (int j = issued_v - 1; j >= 0 && j >= issued_v - C::STAGES; --j)
-          mbar_wait_timeout(bar_v_full + (j % C::STAGES), (j / C::STAGES) & 1, kWaitLimitNs);
+        for (int j = issued - 1; j >= 0 && j >= issued - C::VS; --j)
+          mbar_wait_timeout(bar_v_full + (j % C::VS), (j / C::VS) & 1, kWaitLimitNs);
       }
     }
   } else if (warp == 1) {
@@ -254,32 +292,36 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const uint32_t q_base = smem_u32(sQ);
       const uint32_t k_base = smem_u32(sK);
       const uint32_t v_base = smem_u32(sV);
+      // Descriptors are built once; each MMA only adds its byte offset (>> 4) to the
+      // 14-bit start-address field. Rebuilding them per MMA (shifts, masks, 64-bit
+      // ors in the single issuing thread) costs more cycles than the MMA itself
+      // and starves the tensor core.
+      const uint64_t dq0 = umma_smem_desc(q_base, 16, 1024);
+      const uint64_t dk0 = umma_smem_desc(k_base, 16, 1024);
+      const uint64_t dv0 = umma_smem_desc(v_base, kBN * 128, 1024);
       auto issue_s = [&](int t, int j) {
-        const int st = j % C::STAGES;
+        const int st = j % C::KS;
         const uint32_t s_col = t ? C::TM_S1 : C::TM_S0;
+        const uint64_t aq = dq0 + static_cast<uint64_t>((t * C::Q_BYTES) >> 4);
+        const uint64_t bk = dk0 + static_cast<uint64_t>((st * C::KV_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const int c = kk >> 2;
-          const uint32_t off = (kk & 3) * 32;
-          const uint64_t adesc =
-              umma_smem_desc(q_base + t * C::Q_BYTES + c * kBM * 128 + off, 16, 1024);
-          const uint64_t bdesc =
-              umma_smem_desc(k_base + st * C::KV_BYTES + c * kBN * 128 + off, 16, 1024);
-          umma_ss(tmem + s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+          constexpr int kRow = kBM * 128;
+          const uint32_t off = ((kk >> 2) * kRow + (kk & 3) * 32) >> 4;
+          umma_ss(tmem + s_col, aq + off, bk + off, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar_s_full + t);
       };
       auto issue_pv = [&](int t, int j) {
-        const int st = j % C::STAGES;
-        const uint32_t p_col = t ? C::TM_S1 : C::TM_S0;
-        const uint32_t o_col = t ? C::TM_O1 : C::TM_O0;
+        const int st = j % C::VS;
+        const uint32_t p_col = tmem + (t ? C::TM_S1 : C::TM_S0);
+        const uint32_t o_col = tmem + (t ? C::TM_O1 : C::TM_O0);
+        const uint64_t bv = dv0 + static_cast<uint64_t>((st * C::KV_BYTES) >> 4);
+        const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bdesc = umma_smem_desc(v_base + st * C::KV_BYTES + kk * 16 * 128,
-                                                kBN * 128, 1024);
-          umma_ts(tmem + o_col, tmem + p_col + kk * 8, bdesc, idesc_o,
-                  (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          umma_ts(o_col, p_col + kk * 8, bv + ((kk * 16 * 128) >> 4), idesc_o,
+                  kk > 0 ? 1u : acc0);
         if (j == n_kv[t] - 1) umma_commit(bar_o_final + t);
       };
 
@@ -292,11 +334,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         umma_commit(bar_k_empty);
       }
       for (int j = 0; ok && j < n_kv_max; ++j) {
-        const int st = j % C::STAGES;
-        const uint32_t ph = (j / C::STAGES) & 1;
+        const int st = j % C::VS;   // V stage of tile j
+        const uint32_t ph = (j / C::VS) & 1;
         const int jn = j + 1;
-        const int stn = jn % C::STAGES;
-        const uint32_t phn = (jn / C::STAGES) & 1;
+        const int stn = jn % C::KS;  // K stage of tile j + 1
+        const uint32_t phn = (jn / C::KS) & 1;
         if (!(ok = mbar_wait_bounded(bar_v_full + st, ph, abort_flag, kWaitLimitNs))) break;
         if (j < n_kv[0]) {
           if (!(ok = mbar_wait_bounded(bar_p_full + 0, j & 1, abort_flag, kWaitLimitNs))) break;
@@ -327,7 +369,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
    }
   } else {
-    reg_alloc<kRegsSoftmax>();
+    reg_alloc<kRegsSoftmax<D>>();
     // ------------------------------------------------ softmax warpgroups
     const int t = (warp - 4) >> 2;       // query tile of this warpgroup
     const int wq = warp & 3;             // TMEM lane quarter this warp may access
@@ -375,26 +417,49 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
+        const int n0 = j * kBN;
+        // a tile that reaches past some row's last visible key takes the masked path
+        const bool masked = __any_sync(0xffffffffu, n0 + kBN - 1 > lim);
+        // Row max in CIE_MAX_CHAINS independent fmax3 chains; with CIE_SPLIT_LD the
+        // second half of the row is loaded from TMEM while the first half is reduced.
+        float mx[CIE_MAX_CHAINS];
+#pragma unroll
+        for (int i = 0; i < CIE_MAX_CHAINS; ++i) mx[i] = -INFINITY;
+        auto reduce_cols = [&](int c0, int c1) {
+          if (masked) {
+#pragma unroll
+            for (int c = c0; c < c1; ++c)
+              if (n0 + c > lim) sv[c] = -INFINITY;
+          }
+#pragma unroll
+          for (int c = c0; c < c1; c += 2) {
+            const int i = ((c - c0) / 2) % CIE_MAX_CHAINS;
+            mx[i] = fmax3(mx[i], sv[c], sv[c + 1]);
+          }
+        };
+#if CIE_SPLIT_LD
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 2; c < 4; ++c)
+          tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
+        reduce_cols(0, 64);
+        tmem_wait_ld();
+        reduce_cols(64, 128);
+#else
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c)
           tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
         tmem_wait_ld();
-
-        const int n0 = j * kBN;
-        // a tile that reaches past some row's last visible key takes the masked path
-        const bool masked = __any_sync(0xffffffffu, n0 + kBN - 1 > lim);
-        if (masked) {
+        reduce_cols(0, 128);
+#endif
 #pragma unroll
-          for (int c = 0; c < kBN; ++c)
-            if (n0 + c > lim) sv[c] = -INFINITY;
-        }
-        float mx0 = fmaxf(sv[0], sv[1]), mx1 = fmaxf(sv[2], sv[3]);
+        for (int w = CIE_MAX_CHAINS / 2; w >= 1; w /= 2)
 #pragma unroll
-        for (int c = 4; c < kBN; c += 4) {
-          mx0 = fmax3(mx0, sv[c], sv[c + 1]);
-          mx1 = fmax3(mx1, sv[c + 2], sv[c + 3]);
-        }
-        const float m_new = fmaxf(m_run, fmaxf(mx0, mx1) * p.scale_log2);
+          for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+        const float m_new = fmaxf(m_run, mx[0] * p.scale_log2);
         if (j == 0) {
           m_run = m_new;  // PV of tile t starts O from zero
         } else {
