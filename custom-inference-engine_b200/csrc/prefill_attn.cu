@@ -25,6 +25,12 @@
 // S_t{j+1} may be issued right behind PV_t_j that still reads P_t from the same
 // columns, and the commit that signals S_t_j complete also covers PV_t_{j-1},
 // which is what lets the softmax rescale O_t without a separate wait.
+// The tensor core accepts about one MMA ahead of the one it executes, so any
+// wait or commit in the issuing thread idles it. Per key tile the issuer
+// therefore commits twice: after S0_{j+1} (softmax 0) and after S1_{j+1} on a
+// ring of "step" barriers that tells softmax 1 its S is ready and tells both
+// TMA producers which K and V stages are free. Readiness of the next K and V
+// tiles is probed between MMAs, where the issuing thread stalls anyway.
 // Causal tile pairs are ordered heaviest first across the grid.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -46,11 +52,6 @@ template <int D>
 constexpr int kRegsCtrl = D >= 128 ? 80 : 64;
 template <int D>
 constexpr int kRegsSoftmax = D >= 128 ? 208 : 216;
-// Optional: every kEmuEvery-th pair of probabilities is exponentiated on the FMA
-// pipe (exp2_poly2) instead of the MUFU unit. Off by default: measured on B200
-// the softmax is issue-bound rather than MUFU-bound (every 4th pair: 1058 ->
-// 844 TFLOP/s at d = 128), so the extra FMA-pipe instructions cost more than the
-// MUFU cycles they free. Build with -DCIE_EMU_EVERY_D128=N / _D64=N to enable.
 #ifndef CIE_KSTAGES_D128
 #define CIE_KSTAGES_D128 3
 #endif
@@ -66,17 +67,6 @@ constexpr int kRegsSoftmax = D >= 128 ? 208 : 216;
 #ifndef CIE_MAX_CHAINS
 #define CIE_MAX_CHAINS 8
 #endif
-#ifndef CIE_SPLIT_LD
-#define CIE_SPLIT_LD 1
-#endif
-#ifndef CIE_EMU_EVERY_D128
-#define CIE_EMU_EVERY_D128 0
-#endif
-#ifndef CIE_EMU_EVERY_D64
-#define CIE_EMU_EVERY_D64 0
-#endif
-template <int D>
-constexpr int kEmuEvery = D >= 128 ? CIE_EMU_EVERY_D128 : CIE_EMU_EVERY_D64;
 constexpr int kBM = 128;         // rows of one query tile; a CTA owns two
 constexpr int kBN = 128;         // keys per K/V tile
 
@@ -89,8 +79,12 @@ struct PfCfg {
   // stages fill the 227 KB of shared memory next to the two Q tiles.
   static constexpr int KS = (D == 64) ? CIE_KSTAGES_D64 : CIE_KSTAGES_D128;
   static constexpr int VS = (D == 64) ? CIE_VSTAGES_D64 : CIE_VSTAGES_D128;
+  // ring of per-key-tile completion barriers; deeper than either stage ring so
+  // that no waiter can see a phase of the same slot one lap later
+  static constexpr int R = 8;
+  static_assert(R > KS && R > VS, "step ring must be deeper than the K/V rings");
   static constexpr int BAR_OFF = 2 * Q_BYTES + (KS + VS) * KV_BYTES;
-  static constexpr int NBARS = 2 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
+  static constexpr int NBARS = 2 + KS + VS + 1 + R + 2 + 2 + 2 + 1;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 /*tmem slot, abort*/ + 1024 /*align*/;
   static constexpr uint32_t TM_S0 = 0, TM_S1 = 128;    // P_t aliases cols [0, 64) of S_t
   static constexpr uint32_t TM_O0 = 256, TM_O1 = 256 + D;
@@ -167,12 +161,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* bar_q_full = bars + 0;
   uint64_t* bar_q_ready = bars + 1;
   uint64_t* bar_k_full = bars + 2;
-  uint64_t* bar_k_empty = bar_k_full + C::KS;
-  uint64_t* bar_v_full = bar_k_empty + C::KS;
-  uint64_t* bar_v_empty = bar_v_full + C::VS;
-  uint64_t* bar_s_full = bar_v_empty + C::VS;  // [2] per tile
-  uint64_t* bar_p_full = bar_s_full + 2;           // [2] per tile
-  uint64_t* bar_o_final = bar_p_full + 2;          // [2] per tile
+  uint64_t* bar_v_full = bar_k_full + C::KS;
+  uint64_t* bar_s0_full = bar_v_full + C::VS;  // S0_j complete (and PV0_{j-1})
+  // bar_step[i % R], phase i / R: every MMA up to S1_i complete. Frees K_i's
+  // stage (S0_i, S1_i done) and V_{i-1}'s stage (PV0_{i-1}, PV1_{i-1} done), and
+  // is softmax 1's "S1_i ready".
+  uint64_t* bar_step = bar_s0_full + 1;
+  uint64_t* bar_pa_full = bar_step + C::R;  // [2] per tile: P_t keys 0..63 written
+  uint64_t* bar_p_full = bar_pa_full + 2;   // [2] per tile: all of P_t written
+  uint64_t* bar_o_final = bar_p_full + 2;   // [2] per tile
   uint64_t* bar_drain = bar_o_final + 2;           // [1] abort path only
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -201,18 +198,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 1);
-    mbar_init(bar_q_ready, 256);
-    for (int s = 0; s < C::KS; ++s) {
-      mbar_init(bar_k_full + s, 1);
-      mbar_init(bar_k_empty + s, 1);
-    }
-    for (int s = 0; s < C::VS; ++s) {
-      mbar_init(bar_v_full + s, 1);
-      mbar_init(bar_v_empty + s, 1);
-    }
+    mbar_init(bar_q_ready, 8);  // one arrive per softmax warp
+    for (int s = 0; s < C::KS; ++s) mbar_init(bar_k_full + s, 1);
+    for (int s = 0; s < C::VS; ++s) mbar_init(bar_v_full + s, 1);
+    mbar_init(bar_s0_full, 1);
+    for (int s = 0; s < C::R; ++s) mbar_init(bar_step + s, 1);
     for (int t = 0; t < 2; ++t) {
-      mbar_init(bar_s_full + t, 1);
-      mbar_init(bar_p_full + t, 128);
+      // one arrive per softmax warp (after its lanes synchronised): four arrivals
+      // complete a phase much sooner than 128 per-thread ones
+      mbar_init(bar_pa_full + t, 4);
+      mbar_init(bar_p_full + t, 4);
       mbar_init(bar_o_final + t, 1);
     }
     mbar_init(bar_drain, 1);
@@ -245,8 +240,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       int issued = 0;
       for (int j = 0; j < n_kv_max; ++j) {
         const int st = j % C::KS;
-        const uint32_t ph = (j / C::KS) & 1;
-        if (!mbar_wait_bounded(bar_k_empty + st, ph ^ 1, abort_flag, kWaitLimitNs)) break;
+        // K_{j-KS} left this stage once S1_{j-KS} completed
+        const int fr = j - C::KS;
+        if (fr >= 0 && !mbar_wait_bounded(bar_step + fr % C::R, (fr / C::R) & 1, abort_flag,
+                                          kWaitLimitNs))
+          break;
         mbar_arrive_expect_tx(bar_k_full + st, C::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < C::KCH; ++c)
@@ -269,8 +267,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       int issued = 0;
       for (int j = 0; j < n_kv_max; ++j) {
         const int st = j % C::VS;
-        const uint32_t ph = (j / C::VS) & 1;
-        if (!mbar_wait_bounded(bar_v_empty + st, ph ^ 1, abort_flag, kWaitLimitNs)) break;
+        // V_{j-VS} left this stage once PV1_{j-VS} completed, i.e. by step j-VS+1
+        const int fr = j - C::VS + 1;
+        if (j >= C::VS && !mbar_wait_bounded(bar_step + fr % C::R, (fr / C::R) & 1, abort_flag,
+                                             kWaitLimitNs))
+          break;
         mbar_arrive_expect_tx(bar_v_full + st, C::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < C::KCH; ++c)
@@ -285,21 +286,31 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
-    if (lane == 0 && n_kv_max > 0) {
+    // The whole warp runs the issue loop (waits, probes, control flow) and one
+    // elected lane issues each tcgen05 instruction. Measured on B200 with the
+    // loop on a single lane instead, the per-group commits and waits cost ~40%
+    // of the tensor core's throughput (91 instead of 64 cycles per MMA).
+    if (n_kv_max > 0) {
       constexpr int fmt = BF16 ? 1 : 0;
       constexpr uint32_t idesc_s = umma_idesc_f16(kBM, kBN, fmt, 0, 0);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBM, D, fmt, 0, 1);
-      const uint32_t q_base = smem_u32(sQ);
-      const uint32_t k_base = smem_u32(sK);
-      const uint32_t v_base = smem_u32(sV);
       // Descriptors are built once; each MMA only adds its byte offset (>> 4) to the
-      // 14-bit start-address field. Rebuilding them per MMA (shifts, masks, 64-bit
-      // ors in the single issuing thread) costs more cycles than the MMA itself
-      // and starves the tensor core.
-      const uint64_t dq0 = umma_smem_desc(q_base, 16, 1024);
-      const uint64_t dk0 = umma_smem_desc(k_base, 16, 1024);
-      const uint64_t dv0 = umma_smem_desc(v_base, kBN * 128, 1024);
-      auto issue_s = [&](int t, int j) {
+      // 14-bit start-address field.
+      const uint64_t dq0 = umma_smem_desc(smem_u32(sQ), 16, 1024);
+      const uint64_t dk0 = umma_smem_desc(smem_u32(sK), 16, 1024);
+      const uint64_t dv0 = umma_smem_desc(smem_u32(sV), kBN * 128, 1024);
+      auto commit = [](uint64_t* bar) {
+        if (elect_one_sync()) umma_commit(bar);
+      };
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, kWaitLimitNs));
+      };
+      auto test = [](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_test(bar, parity));
+      };
+      // `probe` runs after the fifth MMA of a group, while the warp waits for the
+      // tensor core to accept the rest
+      auto issue_s = [&](int t, int j, auto&& probe) {
         const int st = j % C::KS;
         const uint32_t s_col = t ? C::TM_S1 : C::TM_S0;
         const uint64_t aq = dq0 + static_cast<uint64_t>((t * C::Q_BYTES) >> 4);
@@ -308,62 +319,79 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int kk = 0; kk < D / 16; ++kk) {
           constexpr int kRow = kBM * 128;
           const uint32_t off = ((kk >> 2) * kRow + (kk & 3) * 32) >> 4;
-          umma_ss(tmem + s_col, aq + off, bk + off, idesc_s, kk > 0 ? 1u : 0u);
+          if (elect_one_sync()) umma_ss(tmem + s_col, aq + off, bk + off, idesc_s, kk > 0 ? 1u : 0u);
+          if (kk == 4) probe();
         }
-        umma_commit(bar_s_full + t);
       };
-      auto issue_pv = [&](int t, int j) {
+      // O_t += P_t V_j in two halves of 64 keys, each behind its half of P
+      auto issue_pv = [&](int t, int j, auto&& probe) {
         const int st = j % C::VS;
         const uint32_t p_col = tmem + (t ? C::TM_S1 : C::TM_S0);
         const uint32_t o_col = tmem + (t ? C::TM_O1 : C::TM_O0);
         const uint64_t bv = dv0 + static_cast<uint64_t>((st * C::KV_BYTES) >> 4);
         const uint32_t acc0 = j > 0 ? 1u : 0u;
+        if (!wait(bar_pa_full + t, j & 1)) return false;
+        tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          umma_ts(o_col, p_col + kk * 8, bv + ((kk * 16 * 128) >> 4), idesc_o,
-                  kk > 0 ? 1u : acc0);
-        if (j == n_kv[t] - 1) umma_commit(bar_o_final + t);
+        for (int kk = 0; kk < kBN / 32; ++kk) {
+          if (elect_one_sync())
+            umma_ts(o_col, p_col + kk * 8, bv + ((kk * 16 * 128) >> 4), idesc_o,
+                    kk > 0 ? 1u : acc0);
+          if (kk == 2) probe();
+        }
+        if (!wait(bar_p_full + t, j & 1)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = kBN / 32; kk < kBN / 16; ++kk) {
+          if (elect_one_sync())
+            umma_ts(o_col, p_col + kk * 8, bv + ((kk * 16 * 128) >> 4), idesc_o, 1u);
+        }
+        if (j == n_kv[t] - 1) commit(bar_o_final + t);
+        return true;
       };
+      auto no_probe = [] {};
 
-      bool ok = mbar_wait_bounded(bar_q_ready, 0, abort_flag, kWaitLimitNs) &&
-                mbar_wait_bounded(bar_k_full, 0, abort_flag, kWaitLimitNs);
+      bool ok = wait(bar_q_ready, 0) && wait(bar_k_full, 0);
       if (ok) {
         tc_fence_after();
-        if (n_kv[0] > 0) issue_s(0, 0);
-        if (n_kv[1] > 0) issue_s(1, 0);
-        umma_commit(bar_k_empty);
+        if (n_kv[0] > 0) {
+          issue_s(0, 0, no_probe);
+          commit(bar_s0_full);
+        }
+        if (n_kv[1] > 0) issue_s(1, 0, no_probe);
+        commit(bar_step);
       }
+      bool v_seen = false;  // V_j's barrier already observed complete
       for (int j = 0; ok && j < n_kv_max; ++j) {
-        const int st = j % C::VS;   // V stage of tile j
-        const uint32_t ph = (j / C::VS) & 1;
         const int jn = j + 1;
         const int stn = jn % C::KS;  // K stage of tile j + 1
         const uint32_t phn = (jn / C::KS) & 1;
-        if (!(ok = mbar_wait_bounded(bar_v_full + st, ph, abort_flag, kWaitLimitNs))) break;
-        if (j < n_kv[0]) {
-          if (!(ok = mbar_wait_bounded(bar_p_full + 0, j & 1, abort_flag, kWaitLimitNs))) break;
-          tc_fence_after();
-          issue_pv(0, j);
-        }
+        bool k_seen = false;
+        if (!v_seen && !(ok = wait(bar_v_full + j % C::VS, (j / C::VS) & 1))) break;
+        if (j < n_kv[0] && !(ok = issue_pv(0, j, [&] {
+              if (jn < n_kv_max) k_seen = test(bar_k_full + stn, phn);
+            })))
+          break;
         if (jn < n_kv_max) {
-          if (!(ok = mbar_wait_bounded(bar_k_full + stn, phn, abort_flag, kWaitLimitNs))) break;
-          tc_fence_after();
-          if (jn < n_kv[0]) issue_s(0, jn);
+          if (!k_seen && !(ok = wait(bar_k_full + stn, phn))) break;
+          if (jn < n_kv[0]) {
+            issue_s(0, jn, no_probe);
+            commit(bar_s0_full);
+          }
         }
-        if (j < n_kv[1]) {
-          if (!(ok = mbar_wait_bounded(bar_p_full + 1, j & 1, abort_flag, kWaitLimitNs))) break;
-          tc_fence_after();
-          issue_pv(1, j);
-        }
-        umma_commit(bar_v_empty + st);
+        v_seen = false;
+        auto probe_v = [&] {
+          if (jn < n_kv_max) v_seen = test(bar_v_full + jn % C::VS, (jn / C::VS) & 1);
+        };
+        if (j < n_kv[1] && !(ok = issue_pv(1, j, probe_v))) break;
         if (jn < n_kv_max) {
-          if (jn < n_kv[1]) issue_s(1, jn);
-          umma_commit(bar_k_empty + stn);
+          if (jn < n_kv[1]) issue_s(1, jn, no_probe);
+          commit(bar_step + jn % C::R);
         }
       }
       if (!ok) {
-        raise_status(CIE_DEV_TIMEOUT);
-        umma_commit(bar_drain);  // all MMAs issued so far must finish before TMEM is freed
+        if (lane == 0) raise_status(CIE_DEV_TIMEOUT);
+        commit(bar_drain);  // all MMAs issued so far must finish before TMEM is freed
         mbar_wait_timeout(bar_drain, 0, kWaitLimitNs);
       }
     }
@@ -394,7 +422,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         rope_q_row<D, BF16>(sQ + t * C::Q_BYTES, row, pos, p.cos, p.sin);
         fence_proxy_async_smem();
       }
-      mbar_arrive(bar_q_ready);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_q_ready);
     }
 
     if (nkv == 0) {
@@ -413,57 +442,43 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       float l_run = 0.f;
       float sv[kBN];
       for (int j = 0; ok && j < nkv; ++j) {
-        ok = mbar_wait_bounded(bar_s_full + t, j & 1, abort_flag, kWaitLimitNs);
+        ok = t ? mbar_wait_bounded(bar_step + j % C::R, (j / C::R) & 1, abort_flag, kWaitLimitNs)
+               : mbar_wait_bounded(bar_s0_full, j & 1, abort_flag, kWaitLimitNs);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
         const int n0 = j * kBN;
         // a tile that reaches past some row's last visible key takes the masked path
         const bool masked = __any_sync(0xffffffffu, n0 + kBN - 1 > lim);
-        // Row max in CIE_MAX_CHAINS independent fmax3 chains; with CIE_SPLIT_LD the
-        // second half of the row is loaded from TMEM while the first half is reduced.
+        // Row max in CIE_MAX_CHAINS independent fmax3 chains.
         float mx[CIE_MAX_CHAINS];
 #pragma unroll
         for (int i = 0; i < CIE_MAX_CHAINS; ++i) mx[i] = -INFINITY;
-        auto reduce_cols = [&](int c0, int c1) {
+        auto mask_cols = [&](int c0, int c1) {
           if (masked) {
 #pragma unroll
             for (int c = c0; c < c1; ++c)
               if (n0 + c > lim) sv[c] = -INFINITY;
           }
+        };
+        auto reduce_cols = [&](int c0, int c1) {
 #pragma unroll
           for (int c = c0; c < c1; c += 2) {
             const int i = ((c - c0) / 2) % CIE_MAX_CHAINS;
             mx[i] = fmax3(mx[i], sv[c], sv[c + 1]);
           }
         };
-#if CIE_SPLIT_LD
+        auto row_max_scaled = [&]() {
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-          tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
-        tmem_wait_ld();
+          for (int w = CIE_MAX_CHAINS / 2; w >= 1; w /= 2)
 #pragma unroll
-        for (int c = 2; c < 4; ++c)
-          tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
-        reduce_cols(0, 64);
-        tmem_wait_ld();
-        reduce_cols(64, 128);
-#else
-#pragma unroll
-        for (int c = 0; c < kBN / 32; ++c)
-          tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
-        tmem_wait_ld();
-        reduce_cols(0, 128);
-#endif
-#pragma unroll
-        for (int w = CIE_MAX_CHAINS / 2; w >= 1; w /= 2)
-#pragma unroll
-          for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
-        const float m_new = fmaxf(m_run, mx[0] * p.scale_log2);
-        if (j == 0) {
-          m_run = m_new;  // PV of tile t starts O from zero
-        } else {
-          // S_t_j complete implies PV_t_{j-1} complete: O_t may be rescaled now
+            for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+          return mx[0] * p.scale_log2;
+        };
+        // Lazy rescale: only rows whose max grew by more than 2^8 move their
+        // reference; S_t_j complete implies PV_t_{j-1} complete, so O_t may be
+        // rescaled in TMEM here.
+        auto rescale = [&](float m_new) {
           const bool need = m_new > m_run + 8.0f;
           if (__any_sync(0xffffffffu, need)) {
             const float alpha = need ? ex2(m_run - m_new) : 1.0f;
@@ -482,40 +497,73 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               m_run = m_new;
             }
           }
-        }
-        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        // p = 2^(s * scale - m): packed FFMA, then MUFU ex2 for most pairs and
-        // the FMA-pipe polynomial for every kEmuEvery-th pair of unmasked tiles
-        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
-        const uint64_t nm2 = f2_pack(-m_use, -m_use);
-        uint64_t sum2 = f2_pack(0.f, 0.f);
+        };
+        // p = 2^(s * scale - m): packed FFMA, MUFU ex2, packed row sum, bf16/fp16
+        // pack. Staged in groups of 8 pairs (8 FFMA2, then 16 ex2, then sums and
+        // packs): measured on B200 with the softmax register budget this keeps the
+        // MUFU unit busier than the per-pair chain (1255 vs 1385 cycles per row of
+        // 128, against a 1024-cycle MUFU floor).
+        uint64_t sum2a = f2_pack(0.f, 0.f), sum2b = sum2a;
+        // P goes to TMEM 16 columns (32 keys) at a time, which keeps only 16 packed
+        // registers live next to the row of S.
+        auto exp_half = [&](int hb, float m) {
+          const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+          const uint64_t nm2 = f2_pack(-m, -m);
+          uint32_t pk[16];
 #pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
-          uint32_t pk[32];
+          for (int g0 = 0; g0 < 32; g0 += 8) {
+            float e[16];
 #pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const uint64_t x2 = ffma2(f2_pack(sv[hb * 64 + c], sv[hb * 64 + c + 1]), sc2, nm2);
-            uint64_t p2;
-            if (kEmuEvery<D> > 0 && !masked && ((c / 2) % kEmuEvery<D>) == kEmuEvery<D> - 1) {
-              p2 = exp2_poly2(x2);
-            } else {
-              float a, b2;
-              f2_unpack(x2, a, b2);
-              p2 = f2_pack(ex2(a), ex2(b2));
+            for (int i = 0; i < 8; ++i) {
+              const int c = hb * 64 + 2 * (g0 + i);
+              f2_unpack(ffma2(f2_pack(sv[c], sv[c + 1]), sc2, nm2), e[2 * i], e[2 * i + 1]);
             }
-            sum2 = fadd2(sum2, p2);
-            float pa, pb;
-            f2_unpack(p2, pa, pb);
-            pk[c / 2] = pack2<BF16>(pa, pb);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) e[i] = ex2(e[i]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const uint64_t p2 = f2_pack(e[2 * i], e[2 * i + 1]);
+              if (i & 1) sum2b = fadd2(sum2b, p2);
+              else sum2a = fadd2(sum2a, p2);
+              pk[(g0 + i) & 15] = pack2<BF16>(e[2 * i], e[2 * i + 1]);
+            }
+            if (g0 & 8) tmem_st16(tmem + lane_addr + s_col + hb * 32 + (g0 & 16), pk);
           }
-          tmem_st32(tmem + lane_addr + s_col + hb * 32, pk);
-        }
+        };
+        // P is written and announced in two halves of 64 keys so that the tensor
+        // core starts on the first half while the second is exponentiated.
+        auto publish = [&](int hb) {
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive((hb ? bar_p_full : bar_pa_full) + t);
+        };
+
+        // first half of S; the second half's load goes out right behind it and
+        // lands while the first half is reduced
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
+        tmem_wait_ld();
+        mask_cols(0, 64);
+#pragma unroll
+        for (int c = 2; c < 4; ++c)
+          tmem_ld32(tmem + lane_addr + s_col + c * 32, reinterpret_cast<uint32_t*>(sv) + c * 32);
+        reduce_cols(0, 64);
+        tmem_wait_ld();
+        mask_cols(64, 128);
+        reduce_cols(64, 128);
+        const float m_new = fmaxf(m_run, row_max_scaled());
+        if (j == 0) m_run = m_new;  // PV of tile t starts O from zero
+        else rescale(m_new);
+        const float m_use = m_run == -INFINITY ? 0.f : m_run;
+        exp_half(0, m_use);
+        publish(0);
+        exp_half(1, m_use);
+        publish(1);
         float lsum0, lsum1;
-        f2_unpack(sum2, lsum0, lsum1);
+        f2_unpack(fadd2(sum2a, sum2b), lsum0, lsum1);
         l_run += lsum0 + lsum1;
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar_p_full + t);
       }
 
       if (ok) {

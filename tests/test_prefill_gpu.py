@@ -93,6 +93,32 @@ def test_random_vs_oracle(cuda, case, dtype):
     assert_close_attn(to_np(out), ref, what=f"{case} {dtype}")
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_running_max_jumps(cuda, D):
+    """Keys whose scores jump far above everything before them in later key tiles:
+    exercises the lazy rescale of O and the recomputation of a speculatively
+    exponentiated half row (a jump of ~2^10 and one of ~2^40 in the log2 domain)."""
+    import torch
+    from kernels.flash_attention import flash_attention
+
+    B, H, Hk, L = 1, 4, 2, 1000
+    rng = np.random.default_rng(D)
+    u = rng.standard_normal(D).astype(np.float32)
+    u /= np.linalg.norm(u)
+    q = normal(11, (B, H, L, D)) + 2.0 * u
+    k = normal(12, (B, Hk, L, D))
+    v = normal(13, (B, Hk, L, D))
+    spike = 1.1 * np.sqrt(D) * 8.0
+    k[:, :, 517, :] = spike * u          # key tile 4 (of 128 keys)
+    k[:, :, 900, :] = 4.0 * spike * u    # key tile 7
+    k[:, :, 901:, :] *= 0.5
+    t = [to_torch(a, torch.bfloat16, cuda) for a in (q, k, v)]
+    out = flash_attention(*t, causal=True)
+    ref = oracle.attention(*(oracle.bf16_round(a) for a in (q, k, v)), causal=True)
+    assert np.isfinite(to_np(out)).all()
+    assert_close_attn(to_np(out), ref, what=f"max jumps d={D}")
+
+
 def test_no_rope_and_q_positions(cuda):
     import torch
     from kernels.flash_attention import flash_attention
