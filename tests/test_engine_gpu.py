@@ -21,6 +21,8 @@ import json
 import numpy as np
 import pytest
 
+from tests.helpers import assert_close_attn
+
 pytestmark = pytest.mark.gpu
 
 
@@ -225,3 +227,51 @@ def test_speculative_matches_base_loop(cuda):
     spec = _speculative(target, target, prompt, _cache(2, 2, 64, cuda), _cache(2, 2, 64, cuda),
                         12, gamma=4)
     assert spec == base
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_batched_step_matches_per_sequence(cuda, d):
+    """begin_step + attention_forward_batch (one fused append and one attention
+    launch for the whole batch, tables packed once per step) against
+    attention_forward run sequence by sequence on a second cache: batched prefill
+    of fresh prompts, then ragged histories through decode (L=1), speculative
+    verify (L=5) and a chunked-prefill block (L=100)."""
+    import torch
+
+    from engine.attention import attention_forward, attention_forward_batch, begin_step
+    from kernels import build_rope_cache
+
+    hq, hkv = 8, 2
+    rope = build_rope_cache(2048, d, theta=500000.0, device=cuda)
+    g = torch.Generator().manual_seed(d)
+
+    def rnd(*s):
+        return torch.randn(*s, generator=g).to(cuda, torch.bfloat16)
+
+    ca, cb = (_cache(1, hkv, d, cuda, blocks=160, bs=16) for _ in range(2))
+    ta = [ca.new_sequence() for _ in range(3)]
+    tb = [cb.new_sequence() for _ in range(3)]
+
+    def run(L, what):
+        q, k, v = rnd(3, hq, L, d), rnd(3, hkv, L, d), rnd(3, hkv, L, d)
+        step = begin_step(ca, ta, L)
+        out = attention_forward_batch(q, k, v, ca, 0, step, rope=rope)
+        for b in range(3):
+            ref = attention_forward(q[b:b + 1], k[b:b + 1], v[b:b + 1], cb, 0, tb[b], rope=rope)
+            assert_close_attn(out[b:b + 1].float().cpu().numpy(), ref.float().cpu().numpy(),
+                              what=f"{what} seq {b}")
+        assert [t.length for t in ta] == [t.length for t in tb]
+
+    run(96, "batched prefill")           # all histories empty: one tcgen05 launch
+    for b, n in enumerate((0, 40, 171)):  # make the histories ragged
+        if n:
+            k, v = rnd(1, hkv, n, d), rnd(1, hkv, n, d)
+            attention_forward(rnd(1, hq, n, d), k, v, ca, 0, ta[b], rope=rope)
+            attention_forward(rnd(1, hq, n, d), k, v, cb, 0, tb[b], rope=rope)
+    run(1, "decode")
+    run(5, "verify")
+    run(100, "chunked prefill")
+    for b in range(3):
+        ka, va = ca.gather(0, ta[b])
+        kb, vb = cb.gather(0, tb[b])
+        assert torch.equal(ka, kb) and torch.equal(va, vb)

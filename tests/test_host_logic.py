@@ -139,3 +139,39 @@ def test_paged_cache_requires_cuda():
 
     with pytest.raises(RuntimeError, match="CUDA"):
         PagedKVCache(KVCacheConfig(1, 2, 16, 4, 4, device="cpu"))
+
+
+class _HostCache:
+    """The host-side part of PagedKVCache that begin_step uses (the real cache
+    holds its pools on a CUDA device)."""
+
+    def __init__(self, num_blocks, block_size):
+        self.alloc = BlockAllocator(num_blocks, block_size)
+        self.device = torch.device("cpu")
+
+    def device_tables(self, tables):
+        return pack_tables(tables, self.device)
+
+
+def test_begin_step_reserves_and_packs_once():
+    from engine.attention import begin_step
+
+    cache = _HostCache(16, 4)
+    a, b, c = (cache.alloc.new_sequence() for _ in range(3))
+    cache.alloc.reserve(a, 5)
+    a.length = 5
+    cache.alloc.reserve(b, 8)
+    b.length = 8
+    step = begin_step(cache, [a, b, c], 3)
+    assert step.starts == [5, 8, 0]
+    assert [t.length for t in (a, b, c)] == [8, 11, 3]
+    # blocks now cover the new tokens of every sequence
+    assert [len(t.blocks) for t in (a, b, c)] == [2, 3, 1]
+    assert step.kv_lens.tolist() == [8, 11, 3]
+    assert step.start_pos.tolist() == [5, 8, 0]
+    assert step.block_tables.dtype == torch.int32
+    assert step.block_tables.tolist() == [a.blocks + [0], b.blocks, c.blocks + [0, 0]]
+    with pytest.raises(ValueError):
+        begin_step(cache, [a], 0)
+    with pytest.raises(ValueError):
+        begin_step(cache, [], 1)
