@@ -379,32 +379,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for a pair of lanes on the FMA pipe instead of the MUFU unit.
-// Cody-Waite split x = n + f with n = rint(x) (the 1.5 * 2^23 rounding trick)
-// and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial whose coefficients were
-// fitted for this build (Lawson-weighted least squares on Chebyshev nodes,
-// max relative error 7.5e-5 over the interval, below half an ulp of bf16 and
-// fp16); 2^n is added straight into the exponent field. x is clamped at -125 so
-// the exponent stays in the normal range: inputs below give ~2^-125, not 0, so
-// callers keep masked (-inf) scores on the MUFU path.
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
-  float a, b;
-  f2_unpack(x2, a, b);
-  const uint64_t x = f2_pack(fmaxf(a, -125.0f), fmaxf(b, -125.0f));
-  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
-  const uint64_t t = fadd2(x, magic);   // rint(x) in the low mantissa bits
-  const uint64_t f = fsub2(x, fsub2(t, magic));
-  uint64_t p = ffma2(f, f2_pack(0x1.c3f75ep-5f, 0x1.c3f75ep-5f),
-                     f2_pack(0x1.f0de1ap-3f, 0x1.f0de1ap-3f));
-  p = ffma2(p, f, f2_pack(0x1.62f31ap-1f, 0x1.62f31ap-1f));
-  p = ffma2(p, f, f2_pack(0x1.fff692p-1f, 0x1.fff692p-1f));
-  float pa, pb, ta, tb;
-  f2_unpack(p, pa, pb);
-  f2_unpack(t, ta, tb);
-  return f2_pack(__int_as_float(__float_as_int(pa) + (__float_as_int(ta) << 23)),
-                 __int_as_float(__float_as_int(pb) + (__float_as_int(tb) << 23)));
-}
-
 // ---------------------------------------------------------------- packing
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
