@@ -576,7 +576,8 @@ def main():
                 "kv_bytes": w.bytes_total, "l2": "inputs larger than L2",
                 "roofline": {"bound": "hbm", "achieved": ach, "peak": peaks["hbm"],
                              "frac": ach / peaks["hbm"], "unit": "GB/s",
-                             "traffic": _traffic(cfg["name"]), "kernel_ms": kms}}
+                             "traffic": _traffic(cfg["name"]) if world == 1 else None,
+                             "kernel_ms": kms}}
             del w
             torch.cuda.empty_cache()
 
