@@ -6,3 +6,4 @@
 #include "paged_attn.cu"
 #include "paged_noalloc.cu"
 #include "prefill_attn.cu"
+#include "int8_gemm.cu"

@@ -47,6 +47,9 @@ SIGNATURES: dict[str, tuple] = {
     "cie_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64p,
                              _i, _vp, _vp, _i, _vp]),
     "cie_rope": (_i, [_vp, _vp, _i, _i, _i, _i, _i64p, _i64p, _i, _i, _vp, _vp, _i, _vp]),
+    "cie_int8_matmul": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, ctypes.c_int64,
+                             ctypes.c_int64, ctypes.c_int64, _i, _vp, _sz, _vp]),
+    "cie_int8_matmul_workspace": (_sz, [_i, _i, _i]),
     "cie_device_status": (_i, [ctypes.POINTER(ctypes.c_int), _i, _vp]),
     "cie_get_last_error": (_i, [ctypes.c_char_p, _i]),
     "cie_version": (ctypes.c_char_p, []),

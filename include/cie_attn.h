@@ -185,6 +185,22 @@ int cie_rope(const void* x, void* y, int B, int H, int L, int d,
              int dtype, const float* rope_cos, const float* rope_sin,
              int rope_max_pos, void* stream);
 
+/* Weight-only INT8 GEMM (replaces the Triton kernel of kernels/int8_matmul.py:
+ * 17-110, semantics of kernels/ref/int8_matmul_ref.py:31-47):
+ *   y[m, n] = sum_k x[m, k] * w[n, k] * scales[n] (+ bias[n])
+ * x: (M, K) bf16/fp16 (dtype), row stride x_stride_m elements (multiple of 8);
+ * w: (N, K) int8, row stride w_stride_n bytes (multiple of 16);
+ * scales, bias: fp32 (N,) (bias may be NULL); y: (M, N) in x's dtype, row
+ * stride y_stride_m. fp32 accumulation on the tensor cores. A workspace of
+ * cie_int8_matmul_workspace(M, N, K) bytes holds split-K partials (0 when the
+ * output tiles alone fill the GPU). */
+int cie_int8_matmul(const void* x, const void* w, const float* scales,
+                    const float* bias, void* y, int M, int N, int K,
+                    int64_t x_stride_m, int64_t w_stride_n, int64_t y_stride_m,
+                    int dtype, void* workspace, size_t workspace_bytes,
+                    void* stream);
+size_t cie_int8_matmul_workspace(int M, int N, int K);
+
 /* Per-device status word (CIE_DEV_* bits) of the current device. Synchronizes
  * `stream`. If clear != 0 the word is reset to 0 afterwards. */
 int cie_device_status(int* status_out, int clear, void* stream);

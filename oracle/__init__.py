@@ -6,6 +6,7 @@ A numpy restatement of the reference's own CPU path:
 * ``attention``                             kernels/ref/flash_attention_ref.py:8-56
 * ``PagedKVCacheRef`` / ``BlockTableRef``   engine/cache/kv_cache.py:34-194,
                                             engine/cache/block_table.py:6-36
+* ``int8_matmul`` / ``dequantize_int8``     kernels/ref/int8_matmul_ref.py:7-47
 
 Parity is pinned: tests/test_oracle_golden.py checks these functions against
 golden vectors produced by the reference itself (tests/golden/make_golden.py
@@ -25,6 +26,7 @@ from oracle.attention_ref import (
     decode_case_ref,
     prefill_case_ref,
 )
+from oracle.int8_ref import dequantize_int8, int8_matmul
 from oracle.kv_cache_ref import BlockTableRef, PagedKVCacheRef, gather_tables
 
 __all__ = [
@@ -37,4 +39,6 @@ __all__ = [
     "BlockTableRef",
     "PagedKVCacheRef",
     "gather_tables",
+    "dequantize_int8",
+    "int8_matmul",
 ]

@@ -103,3 +103,26 @@ def decode_inputs(case):
         ks.append(normal(s + 2, (L, case["Hkv"], case["d"])))
         vs.append(normal(s + 3, (L, case["Hkv"], case["d"])))
     return qs, ks, vs
+
+
+# weight-only INT8 GEMM (kernels/ref/int8_matmul_ref.py); "group" > 0 uses the
+# reference function's per-group scale layout (oracle only: the GPU entry, like
+# the reference's Triton entry, takes per-channel scales)
+INT8_CASES = {
+    "decode_bias": dict(seed=101, M=3, N=96, K=160, bias=True, group=0),
+    "prefill": dict(seed=102, M=130, N=200, K=256, bias=False, group=0),
+    "per_group": dict(seed=103, M=5, N=64, K=128, bias=False, group=32),
+}
+
+
+def int8_inputs(case):
+    rng = np.random.default_rng(case["seed"])
+    M, N, K = case["M"], case["N"], case["K"]
+    x = bf16(rng.standard_normal((M, K)).astype(np.float32))
+    w = rng.integers(-128, 128, size=(N, K), dtype=np.int8)
+    if case["group"]:
+        scales = rng.uniform(0.001, 0.02, size=(N, K // case["group"])).astype(np.float32)
+    else:
+        scales = rng.uniform(0.001, 0.02, size=(N,)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32) if case["bias"] else None
+    return x, w, scales, bias

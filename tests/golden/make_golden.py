@@ -9,6 +9,7 @@ It imports the reference's own CPU code —
   kernels.ref.build_rope_cache / apply_rotary_ref   (kernels/ref/rope_apply_ref.py)
   kernels.ref.flash_attention_ref                   (kernels/ref/flash_attention_ref.py)
   engine.cache.PagedKVCache / BlockTable            (engine/cache/*.py)
+  kernels.ref.int8_matmul_ref.int8_matmul_ref       (kernels/ref/int8_matmul_ref.py)
 — runs them on seeded inputs (numpy PCG64, so the inputs can be regenerated
 bit-identically anywhere) and writes the results to tests/golden/*.npz.
 Inputs are rounded to bfloat16 first, as the GPU path stores them.
@@ -29,11 +30,13 @@ from tests.golden.inputs import (  # noqa: E402
     ATTN_CASES,
     CFG1,
     DECODE_CASES,
+    INT8_CASES,
     ROPE_TABLE_CASES,
     ROTARY_CASES,
     attn_inputs,
     cfg1_inputs,
     decode_inputs,
+    int8_inputs,
     rotary_inputs,
 )
 
@@ -151,6 +154,16 @@ def main() -> None:
         out[f"life_a_v{layer}"] = ga_v.numpy()
         out[f"life_f_k{layer}"] = gf_k.numpy()
     out["life_log"] = np.frombuffer(json.dumps(log).encode(), dtype=np.uint8)
+
+    # 6) int8_matmul_ref (weight-only INT8 GEMM)
+    from kernels.ref.int8_matmul_ref import int8_matmul_ref
+
+    for name, case in INT8_CASES.items():
+        x, w, scales, bias = int8_inputs(case)
+        y = int8_matmul_ref(torch.from_numpy(x), torch.from_numpy(w), torch.from_numpy(scales),
+                            group_size=case["group"] or None,
+                            bias=torch.from_numpy(bias) if bias is not None else None)
+        out[f"int8_{name}"] = y.numpy()
 
     np.savez_compressed(HERE / "golden.npz", **out)
     total = sum(v.nbytes for v in out.values())

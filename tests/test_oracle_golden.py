@@ -12,6 +12,8 @@ import pytest
 
 import oracle
 from tests.golden.inputs import (
+    INT8_CASES,
+    int8_inputs,
     ATTN_CASES,
     CFG1,
     DECODE_CASES,
@@ -168,3 +170,21 @@ def test_gather_tables_matches_cache_gather():
     out = oracle.gather_tables(cache.k[0], table, np.array(lens), 32)
     for i, t in enumerate(tabs):
         np.testing.assert_array_equal(out[i, :lens[i]], cache.gather(0, t)[0])
+
+
+# reference kernels/ref/int8_matmul_ref.py:31-47 (and tests/quant's dequantize round trip)
+@pytest.mark.parametrize("name", sorted(INT8_CASES))
+def test_int8_matmul_matches_reference(golden, name):
+    case = INT8_CASES[name]
+    x, w, scales, bias = int8_inputs(case)
+    y = oracle.int8_matmul(x, w, scales, group_size=case["group"] or None, bias=bias)
+    np.testing.assert_allclose(y, golden[f"int8_{name}"], rtol=1e-5, atol=1e-5)
+
+
+def test_dequantize_per_group_equals_per_channel_when_uniform():
+    rng = np.random.default_rng(7)
+    w = rng.integers(-128, 128, size=(8, 64), dtype=np.int8)
+    s = rng.uniform(0.01, 0.1, size=8).astype(np.float32)
+    per_group = np.repeat(s[:, None], 4, axis=1)
+    np.testing.assert_array_equal(oracle.dequantize_int8(w, s),
+                                  oracle.dequantize_int8(w, per_group, group_size=16))
