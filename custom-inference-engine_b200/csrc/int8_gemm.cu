@@ -67,6 +67,39 @@ __device__ __forceinline__ uint32_t i8x2_to_f16x2(uint32_t word, int sel) {
   return pack2<BF16>(a, b);
 }
 
+
+// int8 -> fp16x2 in two instructions: with u = b ^ 0x80, the fp16 bit pattern
+// 0x6400 | u is 1024 + u (exact: 10-bit mantissa, one binade), so one byte
+// permute builds two of them and one packed subtract of 1152 leaves b.
+__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t flipped, int sel) {
+  const uint32_t h = __byte_perm(flipped, 0x64646464u, sel ? 0x7372 : 0x7170);
+  uint32_t r;
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
+  return r;
+}
+
+// 16 int8 -> 16 bf16/fp16 as two 16-byte chunks.
+template <bool BF16>
+__device__ __forceinline__ void i8x16_to_f16x16(const uint4 v, uint4& lo, uint4& hi) {
+  if constexpr (!BF16) {
+    const uint4 f = make_uint4(v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u,
+                               v.w ^ 0x80808080u);
+    lo = make_uint4(i8x2_to_h2(f.x, 0), i8x2_to_h2(f.x, 1), i8x2_to_h2(f.y, 0),
+                    i8x2_to_h2(f.y, 1));
+    hi = make_uint4(i8x2_to_h2(f.z, 0), i8x2_to_h2(f.z, 1), i8x2_to_h2(f.w, 0),
+                    i8x2_to_h2(f.w, 1));
+    return;
+  }
+  lo.x = i8x2_to_f16x2<BF16>(v.x, 0);
+  lo.y = i8x2_to_f16x2<BF16>(v.x, 1);
+  lo.z = i8x2_to_f16x2<BF16>(v.y, 0);
+  lo.w = i8x2_to_f16x2<BF16>(v.y, 1);
+  hi.x = i8x2_to_f16x2<BF16>(v.z, 0);
+  hi.y = i8x2_to_f16x2<BF16>(v.z, 1);
+  hi.z = i8x2_to_f16x2<BF16>(v.w, 0);
+  hi.w = i8x2_to_f16x2<BF16>(v.w, 1);
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(kQThreads, 1)
     int8_matmul_kernel(const __grid_constant__ CUtensorMap tm_x,
@@ -184,20 +217,21 @@ __global__ void __launch_bounds__(kQThreads, 1)
       uint8_t* dst = sw16(st);
       // 128 rows x 64 int8: per pass a warp reads 8 rows x 4 chunks of 16 bytes
       // (conflict-free) and writes each chunk as 2 swizzled 16-byte chunks
+      // all loads first (independent), then convert and store: the converter
+      // warps are latency-bound otherwise
+      constexpr int kPass = kQW8 / (128 * 16);
+      uint4 vin[kPass];
 #pragma unroll
-      for (int pass = 0; pass < kQW8 / (128 * 16); ++pass) {
+      for (int pass = 0; pass < kPass; ++pass) {
+        const int idx = pass * 128 + ct;
+        vin[pass] = *reinterpret_cast<const uint4*>(src + (idx >> 2) * kQBK + (idx & 3) * 16);
+      }
+#pragma unroll
+      for (int pass = 0; pass < kPass; ++pass) {
         const int idx = pass * 128 + ct;
         const int row = idx >> 2, c = idx & 3;
-        const uint4 v = *reinterpret_cast<const uint4*>(src + row * kQBK + c * 16);
         uint4 lo, hi;
-        lo.x = i8x2_to_f16x2<BF16>(v.x, 0);
-        lo.y = i8x2_to_f16x2<BF16>(v.x, 1);
-        lo.z = i8x2_to_f16x2<BF16>(v.y, 0);
-        lo.w = i8x2_to_f16x2<BF16>(v.y, 1);
-        hi.x = i8x2_to_f16x2<BF16>(v.z, 0);
-        hi.y = i8x2_to_f16x2<BF16>(v.z, 1);
-        hi.z = i8x2_to_f16x2<BF16>(v.w, 0);
-        hi.w = i8x2_to_f16x2<BF16>(v.w, 1);
+        i8x16_to_f16x16<BF16>(vin[pass], lo, hi);
         uint8_t* drow = dst + row * 128;
         *reinterpret_cast<uint4*>(drow + (((2 * c) ^ (row & 7)) * 16)) = lo;
         *reinterpret_cast<uint4*>(drow + (((2 * c + 1) ^ (row & 7)) * 16)) = hi;
@@ -287,6 +321,11 @@ __global__ void __launch_bounds__(kQThreads, 1)
 // K per stage of the GEMV path: 128 int8 (one 128-byte row per output channel,
 // which TMA streams far faster than 64-byte rows at a 4 KB row pitch).
 constexpr int kGBK = 128;
+// 12 warps: TMA producer, MMA issuer, two idle, eight converters (two per
+// scheduler: the widening is the GEMV's critical path); warps 4..7 also run
+// the epilogue.
+constexpr int kGConvWarps = 8;
+constexpr int kGThreads = 128 + 32 * kGConvWarps;
 
 template <int NT>
 struct GemvCfg {
@@ -306,7 +345,7 @@ struct GemvCfg {
 };
 
 template <bool BF16, int NT>
-__global__ void __launch_bounds__(kQThreads, 1)
+__global__ void __launch_bounds__(kGThreads, 1)
     int8_gemv_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_w, const Int8Params p) {
   using C = GemvCfg<NT>;
@@ -340,7 +379,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
       mbar_init(bar_empty + s, 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(bar_conv + b, 4);
+      mbar_init(bar_conv + b, kGConvWarps);
       mbar_init(bar_free + b, 1);
     }
     mbar_init(bar_acc, 1);
@@ -420,7 +459,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------ converters + epilogue
-    const int ct = threadIdx.x - 128;
+    const int ct = threadIdx.x - 128;  // 0 .. 32 * kGConvWarps - 1
     for (int i = 0; i < nk; ++i) {
       const int st = i % C::STAGES, buf = i & 1;
       ok = __all_sync(0xffffffffu,
@@ -432,20 +471,20 @@ __global__ void __launch_bounds__(kQThreads, 1)
       const uint8_t* src = sw8(st);
       uint8_t* dst = sw16(buf);
       // 128 rows x 128 int8: a warp reads 4 rows x 8 chunks of 16 bytes per pass
+      constexpr int kCT = 32 * kGConvWarps;
+      constexpr int kPass = C::W8 / (kCT * 16);
+      uint4 vin[kPass];
 #pragma unroll
-      for (int pass = 0; pass < C::W8 / (128 * 16); ++pass) {
-        const int idx = pass * 128 + ct;
+      for (int pass = 0; pass < kPass; ++pass) {
+        const int idx = pass * kCT + ct;
+        vin[pass] = *reinterpret_cast<const uint4*>(src + (idx >> 3) * kGBK + (idx & 7) * 16);
+      }
+#pragma unroll
+      for (int pass = 0; pass < kPass; ++pass) {
+        const int idx = pass * kCT + ct;
         const int row = idx >> 3, c = idx & 7;
-        const uint4 v = *reinterpret_cast<const uint4*>(src + row * kGBK + c * 16);
         uint4 lo, hi;
-        lo.x = i8x2_to_f16x2<BF16>(v.x, 0);
-        lo.y = i8x2_to_f16x2<BF16>(v.x, 1);
-        lo.z = i8x2_to_f16x2<BF16>(v.y, 0);
-        lo.w = i8x2_to_f16x2<BF16>(v.y, 1);
-        hi.x = i8x2_to_f16x2<BF16>(v.z, 0);
-        hi.y = i8x2_to_f16x2<BF16>(v.z, 1);
-        hi.z = i8x2_to_f16x2<BF16>(v.w, 0);
-        hi.w = i8x2_to_f16x2<BF16>(v.w, 1);
+        i8x16_to_f16x16<BF16>(vin[pass], lo, hi);
         // 16-bit chunks 2c, 2c+1 of the row: block (chunk >> 3), swizzled in it
         uint8_t* drow = dst + (c >> 2) * (kQBN * 128) + row * 128;
         *reinterpret_cast<uint4*>(drow + ((((2 * c) & 7) ^ (row & 7)) * 16)) = lo;
@@ -458,7 +497,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     if (ok && nk > 0) {
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_acc, 0, abort_flag, kWaitLimitNs));
     }
-    if (ok) {
+    if (ok && warp < 8) {
       tc_fence_after();
       const int wq = warp & 3;
       const int n = n0 + wq * 32 + lane;  // TMEM lane == output channel
@@ -600,7 +639,7 @@ static void launch_gemv(const CUtensorMap& mx, const CUtensorMap& mw, const Int8
   constexpr int smem = GemvCfg<NT>::SMEM;
   auto kern = int8_gemv_kernel<BF16, NT>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  kern<<<dim3(pl.n_tiles, pl.split_k), kQThreads, smem, st>>>(mx, mw, prm);
+  kern<<<dim3(pl.n_tiles, pl.split_k), kGThreads, smem, st>>>(mx, mw, prm);
 }
 
 template <bool BF16>
