@@ -299,6 +299,37 @@ class PagedWorkload:
         return o
 
 
+class Int8Workload:
+    """Weight-only INT8 GEMM of the engine's QKV projection (Llama-3-8B: K=4096,
+    N=(32+2*8)*128=6144) for a decode batch of 64 tokens, int8 weights with
+    per-channel scales, bf16 activations (kernels/int8_matmul.py)."""
+
+    M, N, K = 64, 6144, 4096
+
+    def __init__(self, seed=0):
+        import torch
+
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        self.x = torch.randn(self.M, self.K, device="cuda", generator=g).to(torch.bfloat16)
+        self.w = torch.randint(-128, 128, (self.N, self.K), device="cuda", generator=g,
+                               dtype=torch.int8)
+        self.s = torch.rand(self.N, device="cuda", generator=g) * 0.01
+        self.bytes_total = float(self.N * self.K + self.M * self.K * 2 + self.M * self.N * 2 +
+                                 self.N * 4)
+        self.flops_total = 2.0 * self.M * self.N * self.K
+        self.launches_per_step = 2
+
+    def step(self, events=None):
+        from kernels.int8_matmul import int8_matmul
+
+        if events is not None:
+            events[0].record()
+        y = int8_matmul(self.x, self.w, self.s)
+        if events is not None:
+            events[1].record()
+        return y
+
+
 def time_steps(wl, steps, warmup, world, flush=None):
     """W untimed steps, then exactly K timed steps between barriers; returns
     (max-over-ranks total ms, mean per-launch kernel ms from events)."""
@@ -579,6 +610,23 @@ def main():
                              "traffic": _traffic(cfg["name"]) if world == 1 else None,
                              "kernel_ms": kms}}
             del w
+            torch.cuda.empty_cache()
+
+        if world == 1:
+            flush = l2_flush_buffer()
+            w8 = Int8Workload()
+            n8 = max(20, args.steps // 4)
+            t8, k8 = time_steps(w8, n8, args.warmup, world, flush=flush)
+            workloads["f4_int8_qkv_decode"] = {
+                "value": w8.bytes_total / (t8 / n8 * 1e-3) / 1e9, "unit": "GB/s",
+                "ms_per_step": t8 / n8, "tflops": w8.flops_total / (t8 / n8 * 1e-3) / 1e12,
+                "shape": {"M": w8.M, "N": w8.N, "K": w8.K},
+                "l2": "flushed between iterations (weights < L2)",
+                "roofline": {"bound": "hbm", "achieved": w8.bytes_total / (k8 * 1e-3) / 1e9,
+                             "peak": peaks["hbm"],
+                             "frac": w8.bytes_total / (k8 * 1e-3) / 1e9 / peaks["hbm"],
+                             "unit": "GB/s", "kernel_ms": k8}}
+            del w8, flush
             torch.cuda.empty_cache()
 
     # ---------------- end to end through the public API with host buffers
