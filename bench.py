@@ -366,8 +366,17 @@ def time_steps(wl, steps, warmup, world, flush=None):
 
 # ---------------------------------------------------------------- e2e
 def e2e_prefill(cfg, world, rank, steps, warmup):
-    """Through the public API with host buffers: pinned H2D of this rank's Q/K/V,
-    flash_attention (fused RoPE), all-gather, D2H of the output, every step."""
+    """Through the public API with host buffers, every step: pinned H2D of this
+    rank's Q/K/V, flash_attention (fused RoPE), the all-gather of the outputs
+    (N > 1) and a D2H read of the whole result (each gathered batch element is
+    read back by one rank, b % N).
+
+    The step is pipelined per batch element the way a serving loop would run it:
+    H2D copies on one stream, attention and the all-gather on the compute stream,
+    D2H copies on a third, so the two PCIe directions and the tensor cores work
+    at the same time (events keep each buffer from being overwritten before its
+    consumer is done with it, across steps too).
+    """
     import torch
 
     from engine.head_shard import gather_output, shard_heads
@@ -380,30 +389,62 @@ def e2e_prefill(cfg, world, rank, steps, warmup):
     hq = torch.randn(B, sh.hq, S, d, generator=g).to(torch.bfloat16).pin_memory()
     hk = torch.randn(B, sh.hkv, S, d, generator=g).to(torch.bfloat16).pin_memory()
     hv = torch.randn(B, sh.hkv, S, d, generator=g).to(torch.bfloat16).pin_memory()
-    hout = torch.empty(world, B, sh.hq, S, d, dtype=torch.bfloat16).pin_memory()
+    hout = torch.empty(B, world, sh.hq, S, d, dtype=torch.bfloat16).pin_memory()
     dq, dk, dv = (torch.empty_like(t, device="cuda") for t in (hq, hk, hv))
     cos, sin = build_rope_cache(S, d, theta=THETA, device="cuda")
+    comp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    mine = [b for b in range(B) if b % world == rank]
+
+    def ev():
+        return torch.cuda.Event()
+
+    in_ready = [ev() for _ in range(B)]     # H2D of element b landed
+    in_free = [ev() for _ in range(B)]      # attention of element b no longer reads dq/dk/dv[b]
+    out_ready = [ev() for _ in range(B)]    # gathered output of element b complete
+    out_done = [ev() for _ in range(B)]     # D2H of element b finished
+    for e in in_free + out_done:
+        e.record(comp)
+    keep = [None] * B
 
     def step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        o = flash_attention(dq, dk, dv, True, 1.0 / math.sqrt(d), rope=(cos, sin))
-        full = gather_output(o) if world > 1 else o.unsqueeze(0)
-        hout.copy_(full, non_blocking=True)
+        for b in range(B):
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(in_free[b])
+                dq[b].copy_(hq[b], non_blocking=True)
+                dk[b].copy_(hk[b], non_blocking=True)
+                dv[b].copy_(hv[b], non_blocking=True)
+                in_ready[b].record(s_in)
+            comp.wait_event(in_ready[b])
+            o = flash_attention(dq[b:b + 1], dk[b:b + 1], dv[b:b + 1], True, 1.0 / math.sqrt(d),
+                                rope=(cos, sin))
+            in_free[b].record(comp)
+            full = gather_output(o) if world > 1 else o.unsqueeze(0)  # (W, 1, hq, S, d)
+            out_ready[b].record(comp)
+            if b in mine:
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(out_ready[b])
+                    hout[b].copy_(full[:, 0], non_blocking=True)
+                    out_done[b].record(s_out)
+                full.record_stream(s_out)
+            keep[b] = full
 
     for _ in range(warmup):
         step()
+    torch.cuda.synchronize()
     barrier(world)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
+    s.record(comp)
+    s_in.wait_stream(comp)  # no copy of the timed steps starts before the start event
     for _ in range(steps):
         step()
-    e.record()
+    for b in mine:
+        comp.wait_event(out_done[b])
+    e.record(comp)
     torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e) / steps, world)
     h2d = (hq.numel() + hk.numel() + hv.numel()) * 2 * world
-    d2h = hout.numel() * 2 * world
+    d2h = B * world * sh.hq * S * d * 2  # the whole output, read back once
     return prefill_flops(B, cfg["Hq"], S, d) / (ms * 1e-3) / 1e12, h2d, d2h
 
 
