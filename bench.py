@@ -666,7 +666,8 @@ def main():
                 "roofline": {"bound": "hbm", "achieved": w8.bytes_total / (k8 * 1e-3) / 1e9,
                              "peak": peaks["hbm"],
                              "frac": w8.bytes_total / (k8 * 1e-3) / 1e9 / peaks["hbm"],
-                             "unit": "GB/s", "kernel_ms": k8}}
+                             "unit": "GB/s", "kernel_ms": k8,
+                             "traffic": _traffic("f4_int8_qkv_decode")}}
             del w8, flush
             torch.cuda.empty_cache()
 
