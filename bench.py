@@ -546,11 +546,15 @@ def run_reference(args, world, rank):
 
 def run_only(args, world, rank):
     """One workload, no extras: the command line the ncu captures profile."""
-    cfg = {"cfg2": CFG2, "cfg3": CFG3, "cfg4": HEADLINE, "cfg5": CFG5}[args.only]
+    cfg = {"cfg2": CFG2, "cfg3": CFG3, "cfg4": HEADLINE, "cfg5": CFG5}.get(args.only, {})
     cfg = dict(cfg)
     if args.batch:
         cfg["B"] = args.batch
-    if args.only in ("cfg2", "cfg4"):
+    if args.only == "int8":
+        wl = Int8Workload()
+        unit, work = "GB/s", wl.bytes_total / 1e9
+        cfg = {"name": "f4_int8_qkv_decode", "B": wl.M}
+    elif args.only in ("cfg2", "cfg4"):
         wl = PrefillWorkload(cfg, world, rank)
         unit, work = "TFLOP/s", wl.flops_total / 1e12
     else:
@@ -574,7 +578,7 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--only", choices=["cfg2", "cfg3", "cfg4", "cfg5"],
+    ap.add_argument("--only", choices=["cfg2", "cfg3", "cfg4", "cfg5", "int8"],
                     help="time one workload only (used for ncu captures)")
     ap.add_argument("--batch", type=int, default=0,
                     help="with --only: override the batch size (smaller ncu captures)")
