@@ -670,11 +670,12 @@ static int pick_mt(int R, int d) {
 
 static int auto_split_tokens(int64_t units, int max_len, int d) {
   // Lengths are only known on the device, so partitions are sized from the
-  // table width: about 32 (d <= 64) or 16 (d >= 128) partitions per SM over
-  // the batch if every sequence were full, never below 256 / 1024 tokens (so
-  // the partial-result traffic stays around 1% of the K/V bytes), at most 4096.
+  // table width: about 14 partitions per SM over the batch if every sequence
+  // were full (measured on B200: decode and verify both peak there), never
+  // below 256 / 1024 tokens (so the partial-result traffic stays around 1% of
+  // the K/V bytes), at most 4096.
   const int sms = num_sms();
-  const int per_sm = d >= 128 ? 16 : 32;
+  const int per_sm = 14;
   int64_t want = (static_cast<int64_t>(max_len) * units) / (static_cast<int64_t>(sms) * per_sm);
   const int lo = (d >= 128) ? 1024 : 256;
   if (want < lo) want = lo;
