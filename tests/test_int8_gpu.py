@@ -56,10 +56,15 @@ def test_golden_cases(cuda, golden, name, dtype):
 
 SHAPES = [
     # M, N, K, bias
-    (1, 4096, 4096, False),    # decode, one token: split-K across the GPU
-    (7, 6144, 4096, True),     # decode batch (QKV of a Llama-3-8B layer), split-K
-    (20, 1000, 512, True),     # 32-token GEMV tile, ragged channel tile
-    (40, 384, 4096, False),    # 64-token GEMV tile
+    (1, 4096, 4096, False),    # decode, one token: mma.sync GEMV, x staged in shared memory
+    (7, 6144, 4096, True),     # decode batch (QKV of a Llama-3-8B layer), x staged
+    (2, 512, 65536, False),    # x too large to stage: per-chunk x loads
+    (8, 768, 4096, True),      # 64 KB of x: per-chunk x loads
+    (9, 1000, 1024, True),     # mma.sync GEMV, two token blocks, ragged channel tile
+    (32, 256, 64, False),      # tcgen05 GEMV, a single 64-column chunk
+    (3, 256, 100, True),       # K not a multiple of 64 at small M: tcgen05 GEMV, split-K
+    (20, 1000, 512, True),     # 32-token tcgen05 GEMV tile, ragged channel tile
+    (40, 384, 4096, False),    # 64-token tcgen05 GEMV tile
     (64, 512, 320, False),     # K not a multiple of 64 (zero-filled tail tile)
     (200, 300, 256, True),     # ragged M and N tiles
     (1024, 1024, 1024, False), # enough tiles for no split
