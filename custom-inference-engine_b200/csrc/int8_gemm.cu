@@ -328,19 +328,26 @@ __global__ void __launch_bounds__(kQThreads, 1)
 // a widened shared-memory copy. Each epilogue thread owns one output channel
 // (its scale and bias are per-thread constants) and writes it for every token.
 constexpr int kGBK = 128;
-// 12 warps: TMA producer, MMA issuer, two idle, eight converters (two per
-// TMEM lane quadrant: one per 64-column half of a stage); warps 4..7 also run
-// the epilogue.
+// Warps: TMA producer, MMA issuer, (two idle,) eight converters (two per TMEM
+// lane quadrant, one per 64-column half of a stage), the first four of which
+// also run the epilogue. PER_SM CTAs share an SM: 1 normally (a ~200 KB ring,
+// 12 warps), 2 when the channel tiles alone exceed the SM count (a ~100 KB
+// ring each and 10 warps, so that a wide layer runs in one wave instead of
+// 1.5). The idle pair of the 12-warp form measured ~4 % faster than 10 warps.
 constexpr int kGConvWarps = 8;
-constexpr int kGThreads = 128 + 32 * kGConvWarps;
+template <int PER_SM>
+constexpr int kGConv0 = PER_SM == 1 ? 4 : 2;  // first converter warp
+template <int PER_SM>
+constexpr int kGThreads = 32 * (kGConv0<PER_SM> + kGConvWarps);
 
-template <int NT>
+template <int NT, int PER_SM>
 struct GemvCfg {
   static constexpr int W8 = kQBN * kGBK;         // int8 weights, 16 KB, 128-byte swizzle
   static constexpr int XBLK = NT * 128;          // one 64-column block of x
   static constexpr int XB = 2 * XBLK;            // x rows (B operand)
   static constexpr int STAGE = W8 + XB;
-  static constexpr int STAGES = (200 * 1024) / STAGE > 16 ? 16 : (200 * 1024) / STAGE;
+  static constexpr int RING = (PER_SM == 1 ? 200 : 100) * 1024;
+  static constexpr int STAGES = RING / STAGE > 16 ? 16 : RING / STAGE;
   static constexpr int NA = 3;                   // widened weight buffers in TMEM
   static constexpr int BAR_OFF = STAGES * STAGE;
   static constexpr int NBARS = 2 * STAGES + 2 * NA + 2;
@@ -351,11 +358,11 @@ struct GemvCfg {
   static constexpr int TM_COLS = 256;
 };
 
-template <bool BF16, int NT>
-__global__ void __launch_bounds__(kGThreads, 1)
+template <bool BF16, int NT, int PER_SM>
+__global__ void __launch_bounds__(kGThreads<PER_SM>, PER_SM)
     int8_gemv_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_w, const Int8Params p) {
-  using C = GemvCfg<NT>;
+  using C = GemvCfg<NT, PER_SM>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -461,10 +468,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
         mbar_wait_timeout(bar_drain, 0, kWaitLimitNs);
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= kGConv0<PER_SM>) {
     // ------------------------------------------------ converters + epilogue
     // TMEM lane quadrant (warp % 4) = 32 weight rows; kh = which 64 columns
-    const int quad = warp & 3, kh = (warp - 4) >> 2;
+    const int quad = warp & 3, kh = (warp - kGConv0<PER_SM>) >> 2;
     const int row = quad * 32 + lane;
     const uint32_t t_row = tmem + (static_cast<uint32_t>(quad * 32) << 16) + C::A_COL + kh * 32;
     for (int i = 0; i < nk; ++i) {
@@ -506,7 +513,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
     if (ok && nk > 0) {
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_acc, 0, abort_flag, kWaitLimitNs));
     }
-    if (ok && warp < 8) {
+    if (ok && kh == 0) {
       tc_fence_after();
       const int n = n0 + quad * 32 + lane;  // TMEM lane == output channel
       const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
@@ -743,6 +750,7 @@ struct Int8Plan {
   int m_tiles, n_tiles, k_tiles, split_k, tiles_per_split;
   int tile_m;   // M > 64: tokens per tile (128 / 256)
   int gemv_nt;  // 16 / 32 / 64: decode-sized M on the tcgen05 GEMV
+  int gemv_per_sm;  // tcgen05 GEMV CTAs per SM (1 / 2)
   int mma_nb;   // 1 / 2: M <= CIE_INT8_MMA_MAX_M on the mma.sync GEMV (8 tokens per block)
 };
 
@@ -771,7 +779,8 @@ static Int8Plan int8_plan(int M, int N, int K) {
     pl.m_tiles = 1;
     pl.n_tiles = (N + kQBN - 1) / kQBN;
     pl.k_tiles = (K + kGBK - 1) / kGBK;
-    int split = num_sms() / pl.n_tiles;
+    pl.gemv_per_sm = pl.n_tiles > num_sms() ? 2 : 1;
+    int split = pl.gemv_per_sm * num_sms() / pl.n_tiles;
     const int cap = pl.k_tiles / 2 > 1 ? pl.k_tiles / 2 : 1;
     if (split > cap) split = cap;
     if (split < 1) split = 1;
@@ -825,13 +834,20 @@ static int make_rows_map(CUtensorMap* map, const void* base, CUtensorMapDataType
   return CIE_OK;
 }
 
+template <bool BF16, int NT, int PER_SM>
+static void launch_gemv_k(const CUtensorMap& mx, const CUtensorMap& mw, const Int8Params& prm,
+                          const Int8Plan& pl, cudaStream_t st) {
+  constexpr int smem = GemvCfg<NT, PER_SM>::SMEM;
+  auto kern = int8_gemv_kernel<BF16, NT, PER_SM>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  kern<<<dim3(pl.n_tiles, pl.split_k), kGThreads<PER_SM>, smem, st>>>(mx, mw, prm);
+}
+
 template <bool BF16, int NT>
 static void launch_gemv(const CUtensorMap& mx, const CUtensorMap& mw, const Int8Params& prm,
                         const Int8Plan& pl, cudaStream_t st) {
-  constexpr int smem = GemvCfg<NT>::SMEM;
-  auto kern = int8_gemv_kernel<BF16, NT>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  kern<<<dim3(pl.n_tiles, pl.split_k), kGThreads, smem, st>>>(mx, mw, prm);
+  if (pl.gemv_per_sm == 2) launch_gemv_k<BF16, NT, 2>(mx, mw, prm, pl, st);
+  else launch_gemv_k<BF16, NT, 1>(mx, mw, prm, pl, st);
 }
 
 template <bool BF16, int NB>

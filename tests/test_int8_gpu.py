@@ -65,6 +65,7 @@ SHAPES = [
     (3, 256, 100, True),       # K not a multiple of 64 at small M: tcgen05 GEMV, split-K
     (20, 1000, 512, True),     # 32-token tcgen05 GEMV tile, ragged channel tile
     (40, 384, 4096, False),    # 64-token tcgen05 GEMV tile
+    (24, 20000, 256, True),    # more channel tiles than SMs: two GEMV CTAs per SM, ragged N
     (64, 512, 320, False),     # K not a multiple of 64 (zero-filled tail tile)
     (200, 300, 256, True),     # ragged M and N tiles
     (1024, 1024, 1024, False), # enough tiles for no split
