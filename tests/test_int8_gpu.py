@@ -127,6 +127,11 @@ def test_layouts_and_errors(cuda):
     _check(int8_matmul(xs, w, s).float().cpu().numpy(),
            oracle.int8_matmul(xs.float().cpu().numpy(), w.cpu().numpy(), s.cpu().numpy()),
            "bf16", "strided rows")
+    # a few strided rows: the GEMV that copies x into shared memory row by row
+    xs4 = big[:4, 32:160]
+    _check(int8_matmul(xs4, w, s).float().cpu().numpy(),
+           oracle.int8_matmul(xs4.float().cpu().numpy(), w.cpu().numpy(), s.cpu().numpy()),
+           "bf16", "strided rows, x staged")
     assert int8_matmul(torch.empty(0, 128, device=cuda, dtype=torch.bfloat16), w, s).shape == (0, 256)
     with pytest.raises(RuntimeError):
         int8_matmul(x3.cpu(), w.cpu(), s.cpu())
