@@ -594,6 +594,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--only", choices=["cfg2", "cfg3", "cfg4", "cfg5", "int8"],
                     help="time one workload only (used for ncu captures)")
+    ap.add_argument("--chunks", type=int, default=0,
+                    help="N > 1: batch chunks whose all-gather overlaps the next chunk's "
+                         "attention (0: the measured default)")
     ap.add_argument("--batch", type=int, default=0,
                     help="with --only: override the batch size (smaller ncu captures)")
     args = ap.parse_args()
@@ -617,7 +620,7 @@ def main():
         return
 
     # ---------------- headline
-    wl = PrefillWorkload(HEADLINE, world, rank, chunks=4)
+    wl = PrefillWorkload(HEADLINE, world, rank, chunks=args.chunks or 4)
     clocks = ClockSampler()
     if rank == 0:
         clocks.start()
