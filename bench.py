@@ -620,7 +620,9 @@ def main():
         return
 
     # ---------------- headline
-    wl = PrefillWorkload(HEADLINE, world, rank, chunks=args.chunks or 4)
+    # measured: 4 chunks best at N <= 4 (the gather hides behind later chunks), 1 at N = 8
+    # (the gather dominates and smaller launches only lose waves)
+    wl = PrefillWorkload(HEADLINE, world, rank, chunks=args.chunks or (4 if world <= 4 else 1))
     clocks = ClockSampler()
     if rank == 0:
         clocks.start()
