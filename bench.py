@@ -15,9 +15,14 @@ algorithmic K/V bytes), each with its roofline fraction.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-``--impl reference`` times the reference's own CPU algorithm (the numpy
-restatement in oracle/, all host threads) on a bounded sample of the headline
-workload and prints the same line with "impl": "reference".
+``--impl reference`` times the reference's own CPU path (its torch
+``kernels.ref`` RoPE + fp32 attention, imported unmodified from the installed
+reference, all host threads) on bounded samples of the headline workload and
+prints the same line with "impl": "reference". ``cpu_baseline`` (and one per
+secondary workload) times the same code, plus the reference's
+``PagedKVCache.gather`` for the paged workloads, at 1 thread and at all cores.
+Without an installed reference both fall back to the numpy restatement in
+oracle/ and say so ("kind": "port").
 """
 
 from __future__ import annotations
@@ -36,9 +41,34 @@ from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
 PKG = REPO / "custom-inference-engine_b200"
-for _p in (str(REPO), str(PKG)):
-    if _p not in sys.path:
-        sys.path.insert(0, _p)
+REF_ENV = "CIE_REFERENCE_ENGINE"
+
+
+def reference_root() -> Path | None:
+    """The installed reference (its ``kernels`` and ``engine`` packages), or None."""
+    cands = [Path(os.environ[REF_ENV])] if os.environ.get(REF_ENV) else []
+    cands.append(REPO / "baseline" / "_ref")
+    for c in cands:
+        if (c / "kernels" / "ref" / "rope_apply_ref.py").is_file() and \
+                (c / "engine" / "cache" / "kv_cache.py").is_file():
+            return c
+    return None
+
+
+def _path_product():
+    """This repo's package (kernels, engine) on sys.path."""
+    for p in (str(REPO), str(PKG)):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+
+
+def _path_reference(root: Path | None):
+    """The reference's own packages (not this repo's) on sys.path; the oracle
+    (under REPO) stays importable for the fallback."""
+    if str(REPO) not in sys.path:
+        sys.path.insert(0, str(REPO))
+    if root is not None and str(root) not in sys.path:
+        sys.path.insert(0, str(root))
 
 BASELINE = json.loads((REPO / "BASELINE.json").read_text())
 METRIC = BASELINE["metric"]
@@ -192,24 +222,76 @@ class PrefillWorkload:
     def __init__(self, cfg, world, rank, seed=0, chunks=1):
         import torch
 
-        from engine.head_shard import shard_heads
+        from engine.head_shard import local_heads, shard_heads
         from kernels import build_rope_cache
 
         self.cfg, self.world, self.rank = cfg, world, rank
         B, S, d = cfg["B"], cfg["S"], cfg["d"]
         self.shard = shard_heads(cfg["Hq"], cfg["Hkv"], world, rank)
-        g = torch.Generator(device="cuda").manual_seed(seed * 1000 + rank)
-        hq, hkv = self.shard.hq, self.shard.hkv
-        self.q = torch.randn(B, hq, S, d, device="cuda", generator=g).to(torch.bfloat16)
-        self.k = torch.randn(B, hkv, S, d, device="cuda", generator=g).to(torch.bfloat16)
-        self.v = torch.randn(B, hkv, S, d, device="cuda", generator=g).to(torch.bfloat16)
+        self.seed = seed
+        q, k, v = self.full_inputs()
+        # this rank's heads only (the full tensors are drawn identically on every
+        # rank so that the gathered output can be checked against one GPU's)
+        self.q = local_heads(q, self.shard, kv=False).contiguous()
+        self.k = local_heads(k, self.shard, kv=True).contiguous()
+        self.v = local_heads(v, self.shard, kv=True).contiguous()
+        del q, k, v
         self.cos, self.sin = build_rope_cache(S, d, theta=THETA, device="cuda")
         self.scale = 1.0 / math.sqrt(d)
         self.out = torch.empty_like(self.q)
         self.chunks = chunks if world > 1 else 1
+        if self.chunks < 1 or B % self.chunks:
+            raise ValueError(f"--chunks {self.chunks} must divide the batch ({B})")
         self.flops_total = prefill_flops(B, cfg["Hq"], S, d)
         self.launches_per_step = 2  # rope(K) + attention
         self.kernel_ms = []
+
+    def full_inputs(self):
+        """All heads' Q, K, V (bf16, seeded, the same on every rank)."""
+        import torch
+
+        c = self.cfg
+        g = torch.Generator(device="cuda").manual_seed(self.seed * 1000 + 17)
+        shape_q = (c["B"], c["Hq"], c["S"], c["d"])
+        shape_kv = (c["B"], c["Hkv"], c["S"], c["d"])
+        return (torch.randn(shape_q, device="cuda", generator=g).to(torch.bfloat16),
+                torch.randn(shape_kv, device="cuda", generator=g).to(torch.bfloat16),
+                torch.randn(shape_kv, device="cuda", generator=g).to(torch.bfloat16))
+
+    def assemble(self, outs):
+        """The step's output in global head order, (B, Hq, S, d)."""
+        import torch
+
+        if self.world == 1:
+            return torch.cat(outs, 0)
+        g = torch.cat(outs, 1)                     # (W, B, hq, S, d), rank-major
+        W, B, hq, S, d = g.shape
+        return g.permute(1, 0, 2, 3, 4).reshape(B, W * hq, S, d)
+
+    def check_against_one_gpu(self):
+        """N > 1: the gathered output of one step must equal, bit for bit, the
+        output of the whole problem on one GPU (every head runs the same kernel
+        on the same inputs). Every rank takes the step; rank 0 compares."""
+        import torch
+
+        from kernels.flash_attention import apply_rotary, flash_attention
+
+        got = self.assemble(self.step())
+        torch.cuda.synchronize()
+        res = None
+        if self.rank == 0:
+            q, k, v = self.full_inputs()
+            want = flash_attention(q, apply_rotary(k, self.cos, self.sin), v, True, self.scale,
+                                   rope=(self.cos, self.sin), rope_k=False)
+            diff = (got.float() - want.float()).abs()
+            res = {"bit_exact": bool(torch.equal(got, want)),
+                   "max_abs_diff": float(diff.nan_to_num(nan=float("inf")).max()),
+                   "what": "gathered (B, Hq, S, d) output of one step vs the same problem on "
+                           "one GPU"}
+            del q, k, v, want, diff
+        del got
+        torch.cuda.empty_cache()
+        return res
 
     def step(self, events=None):
         """RoPE(K) -> attention (RoPE(Q) in-kernel) -> all-gather (N > 1)."""
@@ -463,97 +545,234 @@ def e2e_prefill(cfg, world, rank, steps, warmup):
 
 
 # ---------------------------------------------------------------- CPU baseline
-def _all_host_threads() -> int:
-    """Let numpy's BLAS use every host core (torchrun sets OMP_NUM_THREADS=1)."""
-    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    try:
-        from threadpoolctl import threadpool_limits
-
-        threadpool_limits(n)
-    except ImportError:
-        pass
-    return n
+def _host_cores() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
 
-def cpu_sample(seconds_target: float = 12.0):
-    """The reference algorithm (numpy oracle, all host threads) on whole query
-    heads of the headline workload: RoPE(q, k) + dense fp32 causal attention,
-    one head at a time, until ~seconds_target of CPU work."""
+def _paged_lens(cfg, seed=0):
+    """The paged workloads' history lengths (same draw as PagedWorkload)."""
     import numpy as np
 
-    import oracle
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(cfg["lo"], cfg["hi"] + 1, size=cfg["B"])
+    return (ctx + cfg["M"]).tolist()
 
-    cores = _all_host_threads()
 
-    cfg = HEADLINE
-    S, d = cfg["S"], cfg["d"]
-    rng = np.random.default_rng(0)
-    c, s = oracle.build_rope_cache(S, d, THETA)
-    k = oracle.bf16_round(rng.standard_normal((1, 1, S, d), dtype=np.float32))
-    v = oracle.bf16_round(rng.standard_normal((1, 1, S, d), dtype=np.float32))
-    kr = oracle.apply_rotary(k, c, s)
-    heads, t0 = 0, time.perf_counter()
+class _CpuPath:
+    """The reference's CPU path for one workload sample, on the host.
+
+    ``backend == "reference"``: the reference's own torch code, imported from its
+    installed copy (kernels/ref/rope_apply_ref.py:6-53 build_rope_cache +
+    apply_rotary_ref, kernels/ref/flash_attention_ref.py:8-56 in fp32, and for
+    the paged workloads engine/cache/kv_cache.py:141-165 PagedKVCache.gather on a
+    CPU cache). ``backend == "port"``: the numpy restatement in oracle/.
+    """
+
+    def __init__(self, backend: str):
+        self.backend = backend
+
+    def prefill(self, cfg, rows=None):
+        """One (batch element, query head) of a prefill config: RoPE(q, k) and
+        causal fp32 attention over the last ``rows`` query rows (default all)."""
+        S, d = cfg["S"], cfg["d"]
+        rows = S if rows is None else rows
+        scale = 1.0 / math.sqrt(d)
+        if self.backend == "reference":
+            import torch
+            from kernels.ref import apply_rotary_ref, build_rope_cache, flash_attention_ref
+
+            g = torch.Generator().manual_seed(0)
+            q = torch.randn(1, 1, rows, d, generator=g).bfloat16().float()
+            k = torch.randn(1, 1, S, d, generator=g).bfloat16().float()
+            v = torch.randn(1, 1, S, d, generator=g).bfloat16().float()
+            cos, sin = build_rope_cache(S, d, theta=THETA)
+            qpos = torch.arange(S - rows, S)
+
+            def step():
+                qr = apply_rotary_ref(q, cos, sin, positions=qpos)
+                kr = apply_rotary_ref(k, cos, sin)
+                flash_attention_ref(qr, kr, v, causal=True, scale=scale)
+        else:
+            import numpy as np
+
+            import oracle
+
+            rng = np.random.default_rng(0)
+            c, s_ = oracle.build_rope_cache(S, d, THETA)
+            q = oracle.bf16_round(rng.standard_normal((1, 1, rows, d), dtype=np.float32))
+            k = oracle.bf16_round(rng.standard_normal((1, 1, S, d), dtype=np.float32))
+            v = oracle.bf16_round(rng.standard_normal((1, 1, S, d), dtype=np.float32))
+
+            def step():
+                qr = oracle.apply_rotary(q, c, s_, np.arange(S - rows, S))
+                kr = oracle.apply_rotary(k, c, s_)
+                oracle.attention(qr, kr, v, causal=True, scale=scale)
+        work = prefill_flops(1, 1, S, d, M=rows, N=S) / 1e12
+        what = (f"{'all' if rows == S else f'last {rows}'} query rows of one (batch, head) of "
+                f"{cfg['name']}")
+        return step, work, "TFLOP/s", what
+
+    def paged(self, cfg, n_seq):
+        """``n_seq`` sequences of a paged config: gather each history from a paged
+        cache, RoPE(q) at its positions, causal fp32 attention of all Hq heads."""
+        lens = _paged_lens(cfg)[:n_seq]
+        Hq, Hkv, M, d, bs = cfg["Hq"], cfg["Hkv"], cfg["M"], cfg["d"], cfg["bs"]
+        scale = 1.0 / math.sqrt(d)
+        if self.backend == "reference":
+            import torch
+            from engine.cache.kv_cache import KVCacheConfig, PagedKVCache
+            from kernels.ref import apply_rotary_ref, build_rope_cache, flash_attention_ref
+
+            nblk = sum((L + bs - 1) // bs for L in lens)
+            cache = PagedKVCache(KVCacheConfig(num_layers=1, num_kv_heads=Hkv, head_dim=d,
+                                               num_blocks=nblk, block_size=bs,
+                                               dtype=torch.bfloat16, device="cpu"))
+            g = torch.Generator().manual_seed(0)
+            tables = []
+            for L in lens:
+                t = cache.new_sequence()
+                cache.append(0, t, torch.randn(L, Hkv, d, generator=g).bfloat16(),
+                             torch.randn(L, Hkv, d, generator=g).bfloat16())
+                tables.append(t)
+            qs = [torch.randn(1, Hq, M, d, generator=g).bfloat16().float() for _ in lens]
+            cos, sin = build_rope_cache(max(lens) + 1, d, theta=THETA)
+
+            def step():
+                for t, q, L in zip(tables, qs, lens):
+                    k, v = cache.gather(0, t)
+                    k = k.float().transpose(0, 1).unsqueeze(0)
+                    v = v.float().transpose(0, 1).unsqueeze(0)
+                    qr = apply_rotary_ref(q, cos, sin, positions=torch.arange(L - M, L))
+                    flash_attention_ref(qr, k, v, causal=True, scale=scale)
+        else:
+            import numpy as np
+
+            import oracle
+
+            rng = np.random.default_rng(0)
+            c, s_ = oracle.build_rope_cache(max(lens) + 1, d, THETA)
+            hist = [(oracle.bf16_round(rng.standard_normal((1, Hkv, L, d), dtype=np.float32)),
+                     oracle.bf16_round(rng.standard_normal((1, Hkv, L, d), dtype=np.float32)))
+                    for L in lens]
+            qs = [oracle.bf16_round(rng.standard_normal((1, Hq, M, d), dtype=np.float32))
+                  for _ in lens]
+
+            def step():
+                for (k, v), q, L in zip(hist, qs, lens):
+                    qr = oracle.apply_rotary(q, c, s_, np.arange(L - M, L))
+                    oracle.attention(qr, k.copy(), v.copy(), causal=True, scale=scale)
+        work = sum(lens) * Hkv * d * 2 * 2 / 1e9
+        return step, work, "GB/s", f"{n_seq} of the {cfg['B']} sequences of {cfg['name']}"
+
+
+def _time_step(step, seconds: float, max_reps: int = 50):
+    step()  # warm-up (allocations, thread pool)
+    reps, t0 = 0, time.perf_counter()
     while True:
-        q = oracle.bf16_round(rng.standard_normal((1, 1, S, d), dtype=np.float32))
-        qr = oracle.apply_rotary(q, c, s)
-        oracle.attention(qr, kr, v, causal=True, scale=1 / math.sqrt(d))
-        heads += 1
+        step()
+        reps += 1
         el = time.perf_counter() - t0
-        if el >= seconds_target or heads >= 32:
-            break
-    # K rotation is shared by the GQA group: charge it once per 4 heads
-    flops = prefill_flops(1, heads, S, d)
-    return {"value": flops / el / 1e12, "unit": "TFLOP/s", "cores": cores,
-            "kind": "port",
-            "sample": f"{heads} query head(s) of configs[3] (batch 0, kv head 0; "
-                      f"{heads}/128 of the workload), numpy oracle, {el:.1f} s"}
+        if el >= seconds or reps >= max_reps:
+            return el / reps
+
+
+CPU_SAMPLES = {"cfg2": ("prefill", CFG2, None), "cfg4": ("prefill", HEADLINE, None),
+               "cfg3": ("paged", CFG3, 8), "cfg5": ("paged", CFG5, 4)}
+
+
+def cpu_worker(names, seconds: float):
+    """Run in a child process whose sys.path holds the reference, not this repo's
+    package: every named CPU sample at 1 thread and at all host cores."""
+    root = reference_root()
+    _path_reference(root)
+    import torch
+
+    path = _CpuPath("reference" if root is not None else "port")
+    cores = _host_cores()
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:
+        threadpool_limits = None
+    out = {}
+    for name in names:
+        kind, cfg, n = CPU_SAMPLES[name]
+        step, work, unit, what = path.prefill(cfg) if kind == "prefill" else path.paged(cfg, n)
+        vals = {}
+        for threads in sorted({1, cores}):
+            torch.set_num_threads(threads)
+            if threadpool_limits is not None:
+                threadpool_limits(threads)
+            vals[threads] = work / _time_step(step, seconds)
+        out[name] = {"unit": unit, "values": vals, "sample": what, "kind": path.backend,
+                     "cores": cores}
+    print(json.dumps(out), flush=True)
+
+
+def cpu_baselines(names, seconds: float = 1.0) -> dict:
+    """The CPU samples, measured in a child process (the reference's packages and
+    this repo's share top-level names, so they cannot share one interpreter)."""
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("OMP_NUM_THREADS", "MKL_NUM_THREADS", "CUDA_VISIBLE_DEVICES")}
+    env["CUDA_VISIBLE_DEVICES"] = ""
+    res = subprocess.run([sys.executable, str(Path(__file__).resolve()), "--cpu-worker",
+                          ",".join(names), "--cpu-seconds", str(seconds)],
+                         capture_output=True, text=True, env=env, timeout=600)
+    if res.returncode != 0:
+        raise RuntimeError(f"CPU baseline worker failed:\n{res.stderr[-2000:]}")
+    raw = json.loads(res.stdout.strip().splitlines()[-1])
+    out = {}
+    for name, r in raw.items():
+        vals = {int(k): v for k, v in r["values"].items()}
+        cores = r["cores"]
+        out[name] = {"value": vals[cores], "unit": r["unit"], "cores": cores,
+                     "value_1_thread": vals[1], "kind": r["kind"],
+                     "sample": r["sample"] + (" (the reference's torch kernels.ref"
+                                              + (" + PagedKVCache.gather" if "paged" in
+                                                 CPU_SAMPLES[name][0] else "")
+                                              + ", installed copy)" if r["kind"] == "reference"
+                                              else " (numpy restatement in oracle/)")
+                     + f"; value at {cores} threads, value_1_thread at 1"}
+    return out
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the reference's CPU algorithm (oracle port) on rank 0."""
+    """--impl reference: the reference's own CPU path on rank 0, all host threads.
+
+    Each step is one (batch element, query head) of the headline workload, the
+    unit the per-step sample scales with: RoPE of q and k and the causal fp32
+    attention, through the reference's kernels.ref (numpy port if the reference
+    is not installed)."""
     if rank != 0:
         return
-    cores = _all_host_threads()
-    import numpy as np
+    root = reference_root()
+    _path_reference(root)
+    import torch
 
-    import oracle
-
-    cfg = HEADLINE
-    S, d = cfg["S"], cfg["d"]
-    rows = 1024  # each step: the last 1024 query rows of one head, against all their keys
-    rng = np.random.default_rng(0)
-    c, s = oracle.build_rope_cache(S, d, THETA)
-    k = oracle.bf16_round(rng.standard_normal((1, 1, S, d), dtype=np.float32))
-    v = oracle.bf16_round(rng.standard_normal((1, 1, S, d), dtype=np.float32))
-    q = oracle.bf16_round(rng.standard_normal((1, 1, rows, d), dtype=np.float32))
-
-    def step():
-        qr = oracle.apply_rotary(q, c, s, np.arange(S - rows, S))
-        kr = oracle.apply_rotary(k, c, s)
-        oracle.attention(qr, kr, v, causal=True, scale=1 / math.sqrt(d))
-
+    cores = _host_cores()
+    torch.set_num_threads(cores)
+    path = _CpuPath("reference" if root is not None else "port")
+    step, work, unit, what = path.prefill(HEADLINE)
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     el = time.perf_counter() - t0
-    flops = prefill_flops(1, 1, S, d, M=rows, N=S)
-    val = flops * args.steps / el / 1e12
+    val = work * args.steps / el
     line = {
-        "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s",
+        "impl": "reference", "metric": METRIC, "value": val, "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": HEADLINE["name"] + " (bounded CPU sample)", "B": 4, "S": S,
-                   "Hq": 32, "Hkv": 8, "d": d},
-        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores,
-                         "kind": "port",
-                         "sample": f"per step: last {rows} query rows of one head of configs[3] "
-                                   "against their visible keys (RoPE + fp32 attention, numpy "
-                                   "restatement of kernels/ref, all host threads)"},
-        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "config": {"workload": HEADLINE["name"] + " (bounded CPU sample per step)",
+                   "B": HEADLINE["B"], "S": HEADLINE["S"], "Hq": HEADLINE["Hq"],
+                   "Hkv": HEADLINE["Hkv"], "d": HEADLINE["d"]},
+        "cpu_baseline": {"value": val, "unit": unit, "cores": cores, "kind": path.backend,
+                         "sample": f"per step: {what}"
+                                   + (" (the reference's torch kernels.ref, installed copy)"
+                                      if path.backend == "reference" else
+                                      " (numpy restatement in oracle/)")},
+        "e2e": {"value": val, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -599,15 +818,21 @@ def main():
                          "attention (0: the measured default)")
     ap.add_argument("--batch", type=int, default=0,
                     help="with --only: override the batch size (smaller ncu captures)")
+    ap.add_argument("--cpu-worker", default="", help=argparse.SUPPRESS)
+    ap.add_argument("--cpu-seconds", type=float, default=1.0, help=argparse.SUPPRESS)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
+    if args.cpu_worker:
+        cpu_worker(args.cpu_worker.split(","), args.cpu_seconds)
+        return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, world, rank)
         return
 
+    _path_product()
     import torch
 
     world, rank, _ = init_dist()
@@ -641,6 +866,7 @@ def main():
             "traffic": traffic if world == 1 else None,
             "kernel": "prefill_attn_kernel<128,bf16> (tcgen05)", "kernel_ms": kern_ms}
     launches = args.steps * (1 + wl.chunks)
+    check = wl.check_against_one_gpu() if world > 1 else None
     del wl
     torch.cuda.empty_cache()
 
@@ -707,7 +933,13 @@ def main():
     status = _lib.device_status(clear=True)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_sample()
+        names = ["cfg4"] + ([] if args.no_secondary else ["cfg2", "cfg3", "cfg5"])
+        cpus = cpu_baselines(names)
+        cpu = cpus.pop("cfg4")
+        for name, c in cpus.items():
+            key = {"cfg2": CFG2, "cfg3": CFG3, "cfg5": CFG5}[name]["name"]
+            if key in workloads:
+                workloads[key]["cpu_baseline"] = c
 
     if rank == 0:
         line = {
@@ -726,6 +958,8 @@ def main():
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": launches, "device_status": status, "workloads": workloads,
         }
+        if check is not None:
+            line["multi_gpu_check"] = check
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

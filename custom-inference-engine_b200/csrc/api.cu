@@ -70,4 +70,16 @@ extern "C" int cie_device_status(int* status_out, int clear, void* stream) {
   return CIE_OK;
 }
 
+extern "C" int cie_set_wait_limit(uint64_t limit_ns, uint64_t* previous_ns) {
+  uint64_t prev = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&prev, g_wait_limit_ns, sizeof(prev));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_wait_limit_ns, &limit_ns, sizeof(limit_ns));
+  if (e != cudaSuccess) {
+    set_error("cie_set_wait_limit: %s", cudaGetErrorString(e));
+    return CIE_ERR_LAUNCH;
+  }
+  if (previous_ns) *previous_ns = prev;
+  return CIE_OK;
+}
+
 extern "C" const char* cie_version(void) { return "cie_attn 0.1.0 sm_100a"; }

@@ -24,8 +24,14 @@ __device__ __forceinline__ void raise_status(unsigned int bits) {
   atomicOr(&g_device_status, bits);
 }
 
-// Upper bound for any single pipeline wait inside a kernel (nanoseconds).
+// Upper bound for any single wait inside a kernel (nanoseconds). Pipeline
+// waits (a role waiting for another role's data or a free stage) read the
+// per-device value g_wait_limit_ns, which starts at this default and can be
+// changed at run time (cie_set_wait_limit); the abort path's drain waits (work
+// already in flight landing before shared memory or TMEM is released) always
+// use the default.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+__device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
 
 // ---------------------------------------------------------------- host side
 void set_error(const char* fmt, ...);

@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
         const int st = i % C::STAGES;
         if (i >= C::STAGES &&
             !mbar_wait_bounded(bar_empty + st, ((i / C::STAGES) - 1) & 1, abort_flag,
-                               kWaitLimitNs))
+                               &g_wait_limit_ns))
           break;
         mbar_arrive_expect_tx(bar_full + st, C::STAGE);
         const int k = (kt0 + i) * kQBK;
@@ -207,9 +207,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
         const int st = i % C::STAGES, b = i % C::NA;
         ok = __all_sync(0xffffffffu,
                         mbar_wait_bounded(bar_full + st, (i / C::STAGES) & 1, abort_flag,
-                                          kWaitLimitNs) &&
+                                          &g_wait_limit_ns) &&
                             mbar_wait_bounded(bar_aready + b, (i / C::NA) & 1, abort_flag,
-                                              kWaitLimitNs));
+                                              &g_wait_limit_ns));
         if (!ok) break;
         tc_fence_after();
         const uint32_t a_col = tmem + C::A_COL + b * 32;
@@ -241,9 +241,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
       const int st = i % C::STAGES, b = i % C::NA;
       ok = __all_sync(0xffffffffu,
                       mbar_wait_bounded(bar_full + st, (i / C::STAGES) & 1, abort_flag,
-                                        kWaitLimitNs) &&
+                                        &g_wait_limit_ns) &&
                           (i < C::NA || mbar_wait_bounded(bar_afree + b, ((i / C::NA) - 1) & 1,
-                                                          abort_flag, kWaitLimitNs)));
+                                                          abort_flag, &g_wait_limit_ns)));
       if (!ok) break;
       tc_fence_after();
       // 64-byte swizzle: chunk c of row r sits at chunk c ^ ((r >> 1) & 3); a
@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
       if (lane == 0) mbar_arrive(bar_aready + b);
     }
     if (ok && nk > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_acc, 0, abort_flag, kWaitLimitNs));
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_acc, 0, abort_flag, &g_wait_limit_ns));
     }
     if (ok) {
       tc_fence_after();
@@ -420,7 +420,7 @@ __global__ void __launch_bounds__(kGThreads<PER_SM>, PER_SM)
         const int st = i % C::STAGES;
         if (i >= C::STAGES &&
             !mbar_wait_bounded(bar_empty + st, ((i / C::STAGES) - 1) & 1, abort_flag,
-                               kWaitLimitNs))
+                               &g_wait_limit_ns))
           break;
         mbar_arrive_expect_tx(bar_full + st, C::XB + C::W8);
         const int k = (kt0 + i) * kGBK;
@@ -443,9 +443,9 @@ __global__ void __launch_bounds__(kGThreads<PER_SM>, PER_SM)
         const int st = i % C::STAGES, b = i % C::NA;
         ok = __all_sync(0xffffffffu,
                         mbar_wait_bounded(bar_full + st, (i / C::STAGES) & 1, abort_flag,
-                                          kWaitLimitNs) &&
+                                          &g_wait_limit_ns) &&
                             mbar_wait_bounded(bar_aready + b, (i / C::NA) & 1, abort_flag,
-                                              kWaitLimitNs));
+                                              &g_wait_limit_ns));
         if (!ok) break;
         tc_fence_after();
         const uint32_t a_col = tmem + C::A_COL + b * 64;
@@ -478,9 +478,9 @@ __global__ void __launch_bounds__(kGThreads<PER_SM>, PER_SM)
       const int st = i % C::STAGES, b = i % C::NA;
       ok = __all_sync(0xffffffffu,
                       mbar_wait_bounded(bar_full + st, (i / C::STAGES) & 1, abort_flag,
-                                        kWaitLimitNs) &&
+                                        &g_wait_limit_ns) &&
                           (i < C::NA || mbar_wait_bounded(bar_afree + b, ((i / C::NA) - 1) & 1,
-                                                          abort_flag, kWaitLimitNs)));
+                                                          abort_flag, &g_wait_limit_ns)));
       if (!ok) break;
       tc_fence_after();
       // the 16-byte chunk c of row r sits at chunk c ^ (r & 7) (128-byte swizzle):
@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(kGThreads<PER_SM>, PER_SM)
       if (lane == 0) mbar_arrive(bar_aready + b);
     }
     if (ok && nk > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_acc, 0, abort_flag, kWaitLimitNs));
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_acc, 0, abort_flag, &g_wait_limit_ns));
     }
     if (ok && kh == 0) {
       tc_fence_after();

@@ -6,7 +6,9 @@
 //   * rope_append RoPE of new K rows fused with the scatter of K and V into
 //                 the paged pools (PagedKVCache.append, kv_cache.py:102-139,
 //                 after rope.apply at engine/model/block.py:53-54)
-// All three are HBM-bound: each thread moves 16-byte vectors, consecutive
+//   * copy_blocks whole-block copies inside a pool (PagedKVCache.fork,
+//                 kv_cache.py:169-185)
+// All four are HBM-bound: each thread moves 16-byte vectors, consecutive
 // threads touch consecutive 16-byte chunks of one head row, and grids are
 // sized as a multiple of the SM count.
 #include <cuda_runtime.h>
@@ -159,6 +161,27 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
   }
 }
 
+// ------------------------------------------------------------------ block copy
+// grid.x = block pair, grid.y = slices of the block; each thread moves 16-byte
+// vectors of one physical block of the pool into another.
+__global__ void __launch_bounds__(256) copy_blocks_kernel(uint8_t* __restrict__ pool,
+                                                          const int32_t* __restrict__ src,
+                                                          const int32_t* __restrict__ dst,
+                                                          int num_blocks, int64_t block_bytes) {
+  const int i = blockIdx.x;
+  const int s = src[i], t = dst[i];
+  if (s < 0 || s >= num_blocks || t < 0 || t >= num_blocks) {
+    if (blockIdx.y == 0 && threadIdx.x == 0) raise_status(CIE_DEV_BAD_BLOCK_ID);
+    return;
+  }
+  const uint4* from = reinterpret_cast<const uint4*>(pool + s * block_bytes);
+  uint4* to = reinterpret_cast<uint4*>(pool + t * block_bytes);
+  const int64_t n = block_bytes / 16;
+  for (int64_t w = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x; w < n;
+       w += static_cast<int64_t>(gridDim.y) * blockDim.x)
+    to[w] = from[w];
+}
+
 int rope_launch(const void* x, void* y, int B, int H, int L, int d, const int64_t* xs,
                 const int64_t* ys, int pos0, bool bf16, const float* cos, const float* sin,
                 int max_pos, cudaStream_t st) {
@@ -278,5 +301,32 @@ extern "C" int cie_rope_append(const void* k_new, const void* v_new, void* k_poo
         start_pos, L, Hkv, d, num_blocks, block_size, max_blocks, kv_strides[0], kv_strides[1],
         kv_strides[2], rope_cos, rope_sin, rope_max_pos);
   CIE_CHECK_LAUNCH("rope_append_kernel");
+  return CIE_OK;
+}
+
+extern "C" int cie_copy_blocks(void* const* pools, int n_pools, const int32_t* src_blocks,
+                               const int32_t* dst_blocks, int n, int num_blocks,
+                               size_t block_bytes, void* stream) {
+  CIE_CHECK_ARG(n >= 0 && n_pools >= 0, "cie_copy_blocks: negative count");
+  if (n == 0 || n_pools == 0) return CIE_OK;
+  CIE_CHECK_ARG(pools && src_blocks && dst_blocks, "cie_copy_blocks: null pointer");
+  CIE_CHECK_ARG(num_blocks > 0 && block_bytes > 0 && block_bytes % 16 == 0,
+                "cie_copy_blocks: block size must be a positive multiple of 16 bytes");
+  for (int i = 0; i < n_pools; ++i)
+    CIE_CHECK_ARG(pools[i] && aligned16(pools[i]), "cie_copy_blocks: pool %d null or unaligned",
+                  i);
+  const int threads = 256;
+  const int64_t vec = static_cast<int64_t>(block_bytes / 16);
+  int gy = static_cast<int>((vec + threads - 1) / threads);
+  const int cap = (num_sms() * 8 + n - 1) / n;
+  if (gy > cap) gy = cap < 1 ? 1 : cap;
+  if (gy > 65535) gy = 65535;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  for (int i = 0; i < n_pools; ++i) {
+    copy_blocks_kernel<<<dim3(n, gy), threads, 0, st>>>(reinterpret_cast<uint8_t*>(pools[i]),
+                                                        src_blocks, dst_blocks, num_blocks,
+                                                        static_cast<int64_t>(block_bytes));
+    CIE_CHECK_LAUNCH("copy_blocks_kernel");
+  }
   return CIE_OK;
 }

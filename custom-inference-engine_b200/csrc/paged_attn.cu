@@ -283,6 +283,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
   // K/V prologue first: the copies are in flight while Q is rotated below
   const int my_tiles = n_tiles > warp ? (n_tiles - warp + kPagedWarps - 1) / kPagedWarps : 0;
   int issued = 0;
+  const uint64_t wait_ns = g_wait_limit_ns;  // pipeline wait limit of this launch
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
     if (s < my_tiles) {
@@ -386,7 +387,7 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
     uint8_t* vs = ks + Cfg::kTileBytes;
     const int t0 = tok_begin + (warp + kPagedWarps * it) * kTileTok;
     if constexpr (TMA) {
-      const bool ok = mbar_wait_bounded(wbars + stage, (it / STAGES) & 1, abort_flag, kWaitLimitNs);
+      const bool ok = mbar_wait_bounded(wbars + stage, (it / STAGES) & 1, abort_flag, wait_ns);
       if (!__all_sync(0xffffffffu, ok)) {
         raise_status(CIE_DEV_TIMEOUT);
         break;
@@ -446,7 +447,15 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
 
     // online softmax (log2 domain); O is rescaled only when a row's max grew by > 2^8
     const bool need_mask = (t0 + kTileTok - 1) > lim_min;
+    // fp16: P = p_hi + p_lo, both fp16, so the PV product sees P to about 2^-22
+    // relative instead of one rounding's 2^-12 and the output matches the fp32
+    // reference to within one fp16 rounding (the reference's own fp16 kernel
+    // test asks for 1e-3 where outputs reach |2|, i.e. half an ulp). bf16 keeps a
+    // single rounding: its output ulp (2^-8) dwarfs the P error, and the second
+    // PV MMA measured 10% slower on the verify workload.
+    constexpr bool kSplitP = !BF16;
     uint32_t pa[MT][4];
+    uint32_t pl[kSplitP ? MT : 1][4];
     float alpha[MT][2];
     bool any_rescale = false;
 #pragma unroll
@@ -486,6 +495,12 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
         // A fragment of P: a0/a1 = rows g/g+8, tokens 2t..2t+1; a2/a3 = tokens 8+2t..
         pa[mt][hf] = pack2<BF16>(v[0], v[1]);
         pa[mt][2 + hf] = pack2<BF16>(v[2], v[3]);
+        if constexpr (kSplitP) {
+          const float2 h01 = unpack2<BF16>(pa[mt][hf]);
+          const float2 h23 = unpack2<BF16>(pa[mt][2 + hf]);
+          pl[mt][hf] = pack2<BF16>(v[0] - h01.x, v[1] - h01.y);
+          pl[mt][2 + hf] = pack2<BF16>(v[2] - h23.x, v[3] - h23.y);
+        }
       }
     }
     if (__any_sync(0xffffffffu, any_rescale)) {
@@ -513,6 +528,10 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
       for (int mt = 0; mt < MT; ++mt) {
         mma_16816<BF16>(o_acc[mt][2 * nd], pa[mt], b0, b1);
         mma_16816<BF16>(o_acc[mt][2 * nd + 1], pa[mt], b2, b3);
+        if constexpr (kSplitP) {
+          mma_16816<BF16>(o_acc[mt][2 * nd], pl[mt], b0, b1);
+          mma_16816<BF16>(o_acc[mt][2 * nd + 1], pl[mt], b2, b3);
+        }
       }
     }
     __syncwarp();

@@ -30,11 +30,33 @@ constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
 
 static __device__ __align__(256) unsigned char g_paged_noalloc_scratch[kNoAllocScratchBytes];
 
+typedef CUresult (*PFN_ctxGetCurrent_t)(CUcontext*);
+
+// The driver's cuCtxGetCurrent, resolved once through the runtime (no
+// link-time dependency on libcuda); nullptr if unavailable.
+static PFN_ctxGetCurrent_t ctx_get_current() {
+  static PFN_ctxGetCurrent_t fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_ctxGetCurrent_t>(ptr);
+  });
+  return fn;
+}
+
 // Device address of the scratch array for the current device. Resolved once
-// per device, with that device current, on the first call made on it.
+// per device, with that device current, on the first call made on it, and
+// again whenever the device's current context is not the one the address was
+// resolved in (after cudaDeviceReset the old address is gone; a program that
+// makes its own context current gets that context's copy of the array).
 static int noalloc_scratch(void** out) {
   constexpr int kMaxDevices = 64;
   static void* ptrs[kMaxDevices] = {};
+  static CUcontext ctxs[kMaxDevices] = {};
   static std::mutex mu;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -42,8 +64,13 @@ static int noalloc_scratch(void** out) {
     set_error("cie_paged_attn_noalloc: no usable current device (%s)", cudaGetErrorString(e));
     return CIE_ERR_LAUNCH;
   }
+  // No context yet (or no way to ask) means no cached address can be trusted;
+  // cudaGetSymbolAddress then sets up the device's primary context itself.
+  PFN_ctxGetCurrent_t get_ctx = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (get_ctx != nullptr && get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lock(mu);
-  if (ptrs[dev] == nullptr) {
+  if (ptrs[dev] == nullptr || ctx == nullptr || ctxs[dev] != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_paged_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -51,7 +78,9 @@ static int noalloc_scratch(void** out) {
                 cudaGetErrorString(e));
       return CIE_ERR_LAUNCH;
     }
+    if (get_ctx != nullptr && get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
     ptrs[dev] = p;
+    ctxs[dev] = ctx;
   }
   *out = ptrs[dev];
   return CIE_OK;

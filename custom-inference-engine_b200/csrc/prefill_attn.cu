@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // K_{j-KS} left this stage once S1_{j-KS} completed
         const int fr = j - C::KS;
         if (fr >= 0 && !mbar_wait_bounded(bar_step + fr % C::R, (fr / C::R) & 1, abort_flag,
-                                          kWaitLimitNs))
+                                          &g_wait_limit_ns))
           break;
         mbar_arrive_expect_tx(bar_k_full + st, C::KV_BYTES);
 #pragma unroll
@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // V_{j-VS} left this stage once PV1_{j-VS} completed, i.e. by step j-VS+1
         const int fr = j - C::VS + 1;
         if (j >= C::VS && !mbar_wait_bounded(bar_step + fr % C::R, (fr / C::R) & 1, abort_flag,
-                                             kWaitLimitNs))
+                                             &g_wait_limit_ns))
           break;
         mbar_arrive_expect_tx(bar_v_full + st, C::KV_BYTES);
 #pragma unroll
@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (elect_one_sync()) umma_commit(bar);
       };
       auto wait = [&](uint64_t* bar, uint32_t parity) {
-        return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, kWaitLimitNs));
+        return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, &g_wait_limit_ns));
       };
       auto test = [](uint64_t* bar, uint32_t parity) {
         return __all_sync(0xffffffffu, mbar_test(bar, parity));
@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     bool ok = true;
 
     if (n_kv_max > 0) {
-      ok = mbar_wait_bounded(bar_q_full, 0, abort_flag, kWaitLimitNs);
+      ok = mbar_wait_bounded(bar_q_full, 0, abort_flag, &g_wait_limit_ns);
       ok = __all_sync(0xffffffffu, ok);
       if (ok && p.cos != nullptr && gm < p.M) {
         int pos = p.rope_q_pos0 + gm;
@@ -442,8 +442,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       float l_run = 0.f;
       float sv[kBN];
       for (int j = 0; ok && j < nkv; ++j) {
-        ok = t ? mbar_wait_bounded(bar_step + j % C::R, (j / C::R) & 1, abort_flag, kWaitLimitNs)
-               : mbar_wait_bounded(bar_s0_full, j & 1, abort_flag, kWaitLimitNs);
+        ok = t ? mbar_wait_bounded(bar_step + j % C::R, (j / C::R) & 1, abort_flag, &g_wait_limit_ns)
+               : mbar_wait_bounded(bar_s0_full, j & 1, abort_flag, &g_wait_limit_ns);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
 
       if (ok) {
-        ok = mbar_wait_bounded(bar_o_final + t, 0, abort_flag, kWaitLimitNs);
+        ok = mbar_wait_bounded(bar_o_final + t, 0, abort_flag, &g_wait_limit_ns);
         ok = __all_sync(0xffffffffu, ok);
       }
       if (ok) {

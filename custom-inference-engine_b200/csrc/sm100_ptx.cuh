@@ -98,8 +98,43 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // the wait exceeded `limit_ns` or another thread of the CTA already aborted.
 // Every pipeline wait in the kernels goes through here so that a broken
 // pipeline ends the kernel with a status bit instead of hanging the GPU.
+// The limit is read through a pointer, and only once the first try has
+// failed, so that a run-time setting costs the fast path nothing.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort,
+                                                  const uint64_t* limit_ptr) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t limit_ns = *reinterpret_cast<const volatile uint64_t*>(limit_ptr);
+  if (limit_ns == 0) {
+    // a zero limit: a wait that is not satisfied at once has run out
+    *abort = 1;
+    return false;
+  }
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (((++spins) & 63u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Same, with the limit passed by value (kernels that keep it in a register).
+// A zero limit makes the first probe non-blocking: mbarrier.try_wait suspends
+// the thread for a while in hardware, long enough for a copy in flight to land,
+// so only a non-blocking test lets a zero limit run out reliably.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort, uint64_t limit_ns) {
+  if (limit_ns == 0) {
+    if (mbar_test(bar, parity)) return true;
+    *abort = 1;
+    return false;
+  }
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;

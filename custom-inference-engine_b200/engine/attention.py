@@ -10,11 +10,21 @@ append K/V to the paged cache, attend over the history — done with fused
 kernels: RoPE of K happens inside the paged append, RoPE of q inside the
 attention kernel, and the dense history gather is skipped for decode and
 speculative verify (the paged kernel reads the block table directly).
+
+``fused_attention_forward`` is a drop-in for the whole ``Attention.forward``
+of the reference's decoder block (engine/model/block.py:39-75): the same
+arguments (x, layer_idx, cache, table, positions), the same projections
+(the module's own q/k/v/o ``Int8Linear``s) and the same result, with the
+attention in between done by ``attention_forward``. ``use_fused_attention``
+binds it onto every such module of a model; ``rope_tables`` turns the
+engine's ``RotaryEmbedding`` (whose buffers the runtime casts to fp16,
+engine/runtime.py:22-37) into the fp32 tables the kernels read.
 """
 
 from __future__ import annotations
 
 import math
+import weakref
 from dataclasses import dataclass
 
 import torch
@@ -178,3 +188,99 @@ def attention_forward_batch(
                         hv.transpose(0, 1).unsqueeze(0), True, scale, rope=rope,
                         rope_q_pos0=step.starts[b], rope_k=False))
     return torch.cat(outs, 0)
+
+
+# ------------------------------------------------------------------ drop-in block forward
+_ROPE_CACHE: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+
+
+def rope_tables(rope) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 (cos, sin) tables for the fused kernels.
+
+    ``rope`` is either a ``(cos, sin)`` pair or the engine's ``RotaryEmbedding``
+    (engine/model/rope.py:9-19, buffers ``cos`` / ``sin`` of shape
+    (max_seq_len, head_dim/2)). The engine casts those buffers to the activation
+    dtype (engine/runtime.py:22-37); widening fp16 / bf16 back to fp32 is exact,
+    so the kernels rotate with the very table values the engine's
+    ``apply_rotary_ref`` uses, in fp32 arithmetic. The widened pair is made once
+    per module and reused until its buffers change (another cast or ``.to``).
+    """
+    if isinstance(rope, (tuple, list)):
+        cos, sin = rope
+        if cos.dtype == torch.float32 and sin.dtype == torch.float32:
+            return cos, sin
+        return cos.float().contiguous(), sin.float().contiguous()
+    cos, sin = rope.cos, rope.sin
+    key = (cos.data_ptr(), sin.data_ptr(), cos._version, sin._version, cos.dtype, cos.device)
+    hit = _ROPE_CACHE.get(rope)
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    tabs = (cos.float().contiguous(), sin.float().contiguous()) if cos.dtype != torch.float32 \
+        else (cos.contiguous(), sin.contiguous())
+    _ROPE_CACHE[rope] = (key, tabs)
+    return tabs
+
+
+def _first_position(positions: torch.Tensor | None, table: BlockTable, L: int,
+                    layer_idx: int) -> int:
+    """First absolute position of the new tokens.
+
+    The reference reads ``positions[0]`` with ``.item()`` in every layer
+    (engine/model/block.py:57). TransformerLM hands the same ``positions``
+    tensor to all layers of one forward, so the value is read once per forward
+    and remembered on that tensor; positions held on the host cost no sync.
+    """
+    if positions is None:
+        # layer 0 appends first; later layers see the grown table
+        return table.length if layer_idx == 0 else table.length - L
+    hit = getattr(positions, "_cie_first_position", None)
+    if hit is not None and hit[0] == positions._version:
+        return hit[1]
+    start = int(positions.reshape(-1)[0].item())
+    positions._cie_first_position = (positions._version, start)
+    return start
+
+
+def fused_attention_forward(attn, x: torch.Tensor, layer_idx: int, cache: PagedKVCache,
+                            table: BlockTable, positions: torch.Tensor | None = None
+                            ) -> torch.Tensor:
+    """Drop-in body of the reference's ``Attention.forward`` (engine/model/block.py:39-75).
+
+    ``attn`` is the engine's attention module (its ``q_proj``, ``k_proj``,
+    ``v_proj``, ``o_proj``, ``rope``, ``num_heads``, ``num_kv_heads`` and
+    ``head_dim`` are used as they are). x: (1, L, hidden); positions: (L,)
+    consecutive absolute positions of the new tokens. The projections run as in
+    the reference; RoPE of K is fused into the paged append, RoPE of q into the
+    attention kernel, and decode / verify read the paged history directly (no
+    gather). Returns o_proj(attention) of shape (1, L, hidden), like the
+    reference.
+    """
+    B, L, _ = x.shape
+    if B != 1:
+        raise ValueError("batch size must be 1 (engine/model/block.py:48)")
+    hq, hkv, d = attn.num_heads, attn.num_kv_heads, attn.head_dim
+    q = attn.q_proj(x).view(B, L, hq, d).transpose(1, 2)
+    k = attn.k_proj(x).view(B, L, hkv, d).transpose(1, 2)
+    v = attn.v_proj(x).view(B, L, hkv, d).transpose(1, 2)
+    start = _first_position(positions, table, L, layer_idx)
+    out = attention_forward(q, k, v, cache, layer_idx, table, start=start,
+                            rope=rope_tables(attn.rope), scale=1.0 / math.sqrt(d))
+    out = out.transpose(1, 2).contiguous().view(B, L, hq * d)
+    return attn.o_proj(out)
+
+
+def _is_engine_attention(mod) -> bool:
+    return all(hasattr(mod, a) for a in ("q_proj", "k_proj", "v_proj", "o_proj", "rope",
+                                         "num_heads", "num_kv_heads", "head_dim"))
+
+
+def use_fused_attention(model) -> int:
+    """Route every engine attention module of ``model`` through
+    :func:`fused_attention_forward` (bound per instance; the engine's classes are
+    not modified). Returns the number of modules rerouted."""
+    n = 0
+    for mod in model.modules():
+        if _is_engine_attention(mod):
+            mod.forward = fused_attention_forward.__get__(mod)
+            n += 1
+    return n

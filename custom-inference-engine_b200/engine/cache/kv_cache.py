@@ -10,13 +10,22 @@ free with the same semantics. The data path is native:
   engine/model/block.py:53-64) instead of ceil(L/bs)+1 slice copies;
 * ``gather`` is the bit-exact ``gather_kv`` kernel;
 * ``device_tables`` packs several sequences' block lists into the int32
-  (B, max_blocks) table + (B,) lengths that ``paged_attention`` reads.
+  (B, max_blocks) table + (B,) lengths that ``paged_attention`` reads;
+* ``fork`` copies the blocks with the ``copy_blocks`` kernel (one launch per
+  pool) instead of an index_select + index_copy_ per layer.
 
-Pools live on a CUDA device; there is no CPU data path.
+Block tables reach the device through pinned host buffers and non-blocking
+copies, and a packed table is reused for as long as the sequence's blocks and
+length are unchanged: every layer of one forward step shares the copy the first
+layer made, where the reference builds ``torch.tensor(blocks)`` per layer
+(engine/cache/kv_cache.py:154). Pools live on a CUDA device; there is no CPU
+data path.
 """
 
 from __future__ import annotations
 
+import ctypes
+from collections import OrderedDict
 from dataclasses import dataclass
 
 import torch
@@ -59,6 +68,8 @@ class PagedKVCache:
         self.k = [torch.zeros(shape, dtype=cfg.dtype, device=device) for _ in range(cfg.num_layers)]
         self.v = [torch.zeros(shape, dtype=cfg.dtype, device=device) for _ in range(cfg.num_layers)]
         self.alloc = BlockAllocator(cfg.num_blocks, cfg.block_size)
+        # (kind, key) -> device tensor; small LRU of packed tables / positions
+        self._packed: OrderedDict = OrderedDict()
 
     # --- reference-compatible surface ---
     @property
@@ -84,9 +95,29 @@ class PagedKVCache:
             raise ValueError(f"tensor device/dtype ({t.device}/{t.dtype}) does not match "
                              f"cache ({self.device}/{self.dtype})")
 
+    _PACK_CACHE = 64
+
+    def _cached(self, key, make):
+        hit = self._packed.get(key)
+        if hit is not None:
+            self._packed.move_to_end(key)
+            return hit
+        val = make()
+        self._packed[key] = val
+        if len(self._packed) > self._PACK_CACHE:
+            self._packed.popitem(last=False)
+        return val
+
     def _table_tensor(self, table: BlockTable) -> torch.Tensor:
-        return torch.tensor([table.blocks or [0]], dtype=torch.int32).to(self.device,
-                                                                           non_blocking=True)
+        """int32 (1, n_blocks) device copy of the table's block ids (cached)."""
+        blocks = tuple(table.blocks) or (0,)
+        return self._cached(("blocks", blocks), lambda: _to_device(
+            torch.tensor([blocks], dtype=torch.int32), self.device))
+
+    def _int_tensor(self, value: int) -> torch.Tensor:
+        """int32 (1,) device tensor holding ``value`` (cached)."""
+        return self._cached(("int", int(value)), lambda: _to_device(
+            torch.tensor([int(value)], dtype=torch.int32), self.device))
 
     def append(self, layer: int, table: BlockTable, k: torch.Tensor, v: torch.Tensor,
                start: int | None = None, rope: tuple[torch.Tensor, torch.Tensor] | None = None
@@ -108,9 +139,7 @@ class PagedKVCache:
         self.alloc.reserve(table, end)
         if L > 0:
             rope_append(k.unsqueeze(0), v.unsqueeze(0), self.k[layer], self.v[layer],
-                        self._table_tensor(table),
-                        torch.tensor([start], dtype=torch.int32).to(self.device, non_blocking=True),
-                        rope=rope)
+                        self._table_tensor(table), self._int_tensor(start), rope=rope)
         if end > table.length:
             table.length = end
 
@@ -124,35 +153,68 @@ class PagedKVCache:
             empty = self.k[layer].new_zeros(shape)
             return empty, empty.clone()
         tab = self._table_tensor(table)
-        lens = torch.tensor([L], dtype=torch.int32).to(self.device, non_blocking=True)
+        lens = self._int_tensor(L)
         k = gather_kv(self.k[layer], tab, lens, out_len=L)[0]
         v = gather_kv(self.v[layer], tab, lens, out_len=L)[0]
         return k, v
 
     def fork(self, table: BlockTable) -> BlockTable:
-        """A new BlockTable whose K/V are a deep copy of ``table``'s (kv_cache.py:169-185)."""
+        """A new BlockTable whose K/V are a deep copy of ``table``'s (kv_cache.py:169-185).
+
+        The new blocks come from the LIFO free list in logical order, as in the
+        reference; the data moves with one ``copy_blocks`` launch per pool, fed by
+        block ids copied from pinned memory without a host sync.
+        """
+        from kernels import _lib
+        from kernels.flash_attention import _require, _stream
+
         new_blocks = self.alloc.fork_blocks(table)
-        if new_blocks:
-            src = torch.tensor(table.blocks, dtype=torch.long, device=self.device)
-            dst = torch.tensor(new_blocks, dtype=torch.long, device=self.device)
-            for layer in range(self.cfg.num_layers):
-                self.k[layer].index_copy_(0, dst, self.k[layer].index_select(0, src))
-                self.v[layer].index_copy_(0, dst, self.v[layer].index_select(0, src))
+        n = len(new_blocks)
+        if n:
+            lib = _require()
+            ids = _to_device(torch.tensor([table.blocks, new_blocks], dtype=torch.int32),
+                             self.device)
+            pools = self.k + self.v
+            arr = (ctypes.c_void_p * len(pools))(*[p.data_ptr() for p in pools])
+            block_bytes = self.k[0][0].numel() * self.k[0].element_size()
+            rc = lib.cie_copy_blocks(arr, len(pools), ctypes.c_void_p(ids[0].data_ptr()),
+                                     ctypes.c_void_p(ids[1].data_ptr()), n, self.cfg.num_blocks,
+                                     block_bytes, _stream(self.k[0]))
+            _lib.check(rc, "fork")
         return BlockTable(block_size=self.cfg.block_size, blocks=new_blocks, length=table.length)
 
     def rollback(self, table: BlockTable, new_length: int) -> None:
         self.alloc.rollback(table, new_length)
 
-    def stats(self) -> dict:
+    def stats(self, verbose: bool = True) -> dict:
+        """Footprint and block usage; printed like the reference's ``stats``
+        (engine/cache/kv_cache.py:196-210) and also returned."""
         total = self.cfg.num_blocks
         free = self.alloc.num_free
-        return {"bytes": self.cfg.bytes_required(), "total_blocks": total,
-                "allocated_blocks": total - free, "free_blocks": free}
+        out = {"bytes": self.cfg.bytes_required(), "total_blocks": total,
+               "allocated_blocks": total - free, "free_blocks": free}
+        if verbose:
+            print(f"Cache Memory Footprint: {out['bytes']}")
+            print(f"Total Blocks: {total}")
+            print(f"Allocated Blocks: {total - free}")
+            print(f"Freed Blocks: {free}")
+        return out
 
     # --- batched access for the kernels ---
     def device_tables(self, tables: list[BlockTable]) -> tuple[torch.Tensor, torch.Tensor]:
-        """int32 (B, max_blocks) block table and int32 (B,) lengths on the cache's device."""
-        return pack_tables(tables, self.device)
+        """int32 (B, max_blocks) block table and int32 (B,) lengths on the cache's device.
+
+        Reused while the tables are unchanged (same blocks and lengths), so the
+        layers of one step share a single host-to-device copy."""
+        key = ("tables", tuple((t.length, tuple(t.blocks)) for t in tables))
+        return self._cached(key, lambda: pack_tables(tables, self.device))
+
+
+def _to_device(t: torch.Tensor, device) -> torch.Tensor:
+    """Copy a small host tensor to ``device`` through pinned memory, without a host sync."""
+    if torch.device(device).type == "cuda":
+        return t.pin_memory().to(device, non_blocking=True)
+    return t.to(device)
 
 
 def pack_tables(tables: list[BlockTable], device) -> tuple[torch.Tensor, torch.Tensor]:

@@ -46,11 +46,13 @@ SIGNATURES: dict[str, tuple] = {
     "cie_gather_kv": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "cie_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64p,
                              _i, _vp, _vp, _i, _vp]),
+    "cie_copy_blocks": (_i, [ctypes.POINTER(_vp), _i, _vp, _vp, _i, _i, _sz, _vp]),
     "cie_rope": (_i, [_vp, _vp, _i, _i, _i, _i, _i64p, _i64p, _i, _i, _vp, _vp, _i, _vp]),
     "cie_int8_matmul": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, ctypes.c_int64,
                              ctypes.c_int64, ctypes.c_int64, _i, _vp, _sz, _vp]),
     "cie_int8_matmul_workspace": (_sz, [_i, _i, _i]),
     "cie_device_status": (_i, [ctypes.POINTER(ctypes.c_int), _i, _vp]),
+    "cie_set_wait_limit": (_i, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     "cie_get_last_error": (_i, [ctypes.c_char_p, _i]),
     "cie_version": (ctypes.c_char_p, []),
 }
@@ -104,6 +106,18 @@ def check(rc: int, what: str) -> None:
     if rc == CIE_ERR_UNSUPPORTED:
         raise ValueError(msg)
     raise RuntimeError(msg)
+
+
+DEFAULT_WAIT_LIMIT_NS = 2_000_000_000
+
+
+def set_wait_limit(limit_ns: int) -> int:
+    """Set the in-kernel pipeline wait limit on the current device; returns the old one."""
+    lib = load()
+    prev = ctypes.c_uint64(0)
+    check(lib.cie_set_wait_limit(ctypes.c_uint64(int(limit_ns)), ctypes.byref(prev)),
+          "cie_set_wait_limit")
+    return int(prev.value)
 
 
 def device_status(stream: int = 0, clear: bool = True) -> int:

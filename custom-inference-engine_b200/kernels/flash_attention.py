@@ -30,6 +30,7 @@ import torch
 from kernels import _lib
 
 _DTYPES = {torch.bfloat16: _lib.CIE_DTYPE_BF16, torch.float16: _lib.CIE_DTYPE_FP16}
+_TABLE_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 
 
 def _require() -> ctypes.CDLL:
@@ -52,7 +53,9 @@ def _vp(t: torch.Tensor | None) -> ctypes.c_void_p:
 def _kernel_ready(t: torch.Tensor) -> torch.Tensor:
     """Innermost dim contiguous, other strides multiples of 8 elements, 16B-aligned."""
     if t.stride(-1) != 1 or any(s % 8 for s in t.stride()[:-1]) or t.data_ptr() % 16:
-        t = t.contiguous()
+        # a fresh copy: .contiguous() would return a contiguous view at an
+        # unaligned offset unchanged
+        t = t.clone(memory_format=torch.contiguous_format)
     return t
 
 
@@ -66,8 +69,11 @@ def _rope_tables(rope, device) -> tuple[torch.Tensor | None, torch.Tensor | None
     if rope is None:
         return None, None, 0
     cos, sin = rope
-    if cos.dtype != torch.float32 or sin.dtype != torch.float32:
-        raise ValueError("rope tables must be float32 (max_pos, head_dim/2)")
+    if cos.dtype not in _TABLE_DTYPES or sin.dtype not in _TABLE_DTYPES:
+        raise ValueError("rope tables must be float32, float16 or bfloat16 (max_pos, head_dim/2)")
+    # the kernels read fp32 tables; widening a 16-bit table (e.g. the engine's
+    # RotaryEmbedding buffers after the runtime's cast) is exact
+    cos, sin = cos.float(), sin.float()
     if cos.device != device or sin.device != device:
         raise ValueError("rope tables must live on the same device as q")
     cos = cos.contiguous()

@@ -4,9 +4,14 @@
 (kernels/int8_matmul.py:76-110): y = x @ (w_int8 * scales[:, None]).T (+ bias),
 per-channel fp scales of shape (N,), fp32 accumulation, y in x's dtype, the
 same exception types for bad input (:83-86) and the same shape check (:93).
-bf16 and fp16 activations are both accepted. The int8 weight tile is widened
-to x's dtype in shared memory (exact for int8) and multiplied on tcgen05
-tensor cores; the scale (and bias) are applied once to the fp32 accumulator.
+bf16 and fp16 activations are both accepted. The int8 weights are widened to
+x's dtype in registers (exact for int8) and either held in tensor memory as the
+A operand of tcgen05 MMAs or fed to mma.sync for the smallest batches; the
+scale (and bias) are applied once to the fp32 accumulator, and the result is
+rounded once to x's dtype, as the reference's fp32 formula
+(kernels/ref/int8_matmul_ref.py:31-47) does. The Triton path instead rounds
+x @ w * s to x's dtype and then adds the rounded bias (:107-108), so with a
+bias the two can differ by one unit in the last place of x's dtype.
 """
 
 from __future__ import annotations
@@ -41,12 +46,15 @@ def int8_matmul(
     assert K == K2
     if scales.shape[0] != N:
         raise ValueError(f"scales has {scales.shape[0]} entries for {N} output channels")
+    # The kernels need 16-byte aligned rows; a copy (padded rows when K does not
+    # fill 16 bytes) fixes any other layout, including a contiguous view at an
+    # unaligned offset, which .contiguous() would hand back unchanged.
     if x_2d.stride(1) != 1 or x_2d.stride(0) % 8 or x_2d.data_ptr() % 16:
-        x_2d = x_2d.contiguous()
+        x_2d = x_2d.clone(memory_format=torch.contiguous_format)
         if K % 8:
             x_2d = torch.nn.functional.pad(x_2d, (0, 8 - K % 8))[:, :K]
     if w_int8.stride(1) != 1 or w_int8.stride(0) % 16 or w_int8.data_ptr() % 16:
-        w_int8 = w_int8.contiguous()
+        w_int8 = w_int8.clone(memory_format=torch.contiguous_format)
         if K % 16:
             w_int8 = torch.nn.functional.pad(w_int8, (0, 16 - K % 16))[:, :K]
     s32 = scales.to(device=x.device, dtype=torch.float32).contiguous()

@@ -131,7 +131,10 @@ size_t cie_paged_attn_workspace(int B, int Hq, int Hkv, int M, int d,
  * partials fit; an explicit split_tokens whose partials exceed 32 MiB is
  * rejected with CIE_ERR_WORKSPACE and a message. The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture. The array is
+ * current; make that first call before any stream capture. The address is
+ * kept per device and context and looked up again when the current context
+ * changes (e.g. after cudaDeviceReset); make the first call after such a
+ * change outside stream capture too. The array is
  * shared by all calls on a device and keeps the last call's contents (nothing
  * in it needs to start at zero); calls that overlap on the GPU race on it and
  * must be serialised by the caller. It never calls cudaMalloc or cudaFree.
@@ -176,6 +179,21 @@ int cie_rope_append(const void* k_new, const void* v_new, void* k_pool,
                     int rope_max_pos, void* stream);
 
 /*
+ * Whole-block copies inside paged pools, the data movement of
+ * PagedKVCache.fork (engine/cache/kv_cache.py:169-185, where it is an
+ * index_select + index_copy_ per layer):
+ *   pools[p][dst_blocks[i]] = pools[p][src_blocks[i]]  for i < n, p < n_pools
+ * pools: host array of n_pools device pointers (e.g. the K and V pool of every
+ * layer), each holding num_blocks blocks of block_bytes bytes (a multiple of
+ * 16). src_blocks / dst_blocks: int32 device arrays of n block ids; ids
+ * outside [0, num_blocks) set CIE_DEV_BAD_BLOCK_ID and are skipped. Source
+ * and destination blocks must not overlap. One launch per pool.
+ */
+int cie_copy_blocks(void* const* pools, int n_pools, const int32_t* src_blocks,
+                    const int32_t* dst_blocks, int n, int num_blocks,
+                    size_t block_bytes, void* stream);
+
+/*
  * Standalone half-split RoPE: y[b, h, i, :] = rope(x[b, h, i, :], pos0 + i),
  * computed in fp32 and rounded to the element type
  * (kernels/ref/rope_apply_ref.py:22-53). x, y: (B, H, L, d) with strides.
@@ -204,6 +222,18 @@ size_t cie_int8_matmul_workspace(int M, int N, int K);
 /* Per-device status word (CIE_DEV_* bits) of the current device. Synchronizes
  * `stream`. If clear != 0 the word is reset to 0 afterwards. */
 int cie_device_status(int* status_out, int clear, void* stream);
+
+/* Sets the time limit (nanoseconds) of every pipeline wait inside the kernels
+ * on the current device, for kernels launched after this call; the previous
+ * value is stored in *previous_ns when it is non-NULL. The default is
+ * 2 000 000 000 (2 s). A wait that runs out sets CIE_DEV_TIMEOUT, makes the
+ * kernel's other roles leave their loops, lets copies and MMAs already in
+ * flight land (waits that always use the 2 s default), releases tensor memory
+ * and returns; the outputs of that launch are undefined, the context stays
+ * usable. A limit of 0 makes every wait that is not satisfied at once run
+ * out, which is how the tests reach that path. No counterpart in the
+ * reference (its Triton kernels have no device-side waits). Synchronous. */
+int cie_set_wait_limit(uint64_t limit_ns, uint64_t* previous_ns);
 
 /* Copies the last host-side error message of the calling thread into buf. */
 int cie_get_last_error(char* buf, int buf_len);

@@ -195,3 +195,75 @@ def test_config3_full_size_sampled(cuda):
     ref = ref_paged(q[pick], [ks[i] for i in pick], [vs[i] for i in pick], [lens[i] for i in pick],
                     c, s)
     assert_close_attn(out[pick], ref, what="cfg3 sampled")
+
+
+def _device_pool(lens, Hkv, d, bs, seed, device):
+    """Seeded random bf16 pools built on the device (the full-size configs are too
+    large to assemble on the host) and seeded random-permutation block tables."""
+    import torch
+
+    nblk = [(L + bs - 1) // bs for L in lens]
+    pool = int(sum(nblk))
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(pool).astype(np.int32)
+    tables = np.zeros((len(lens), max(nblk)), np.int32)
+    off = 0
+    for i, n in enumerate(nblk):
+        tables[i, :n] = perm[off: off + n]
+        off += n
+    g = torch.Generator(device=device).manual_seed(seed)
+    kp = torch.randn(pool, bs, Hkv, d, device=device, generator=g).to(torch.bfloat16)
+    vp = torch.randn(pool, bs, Hkv, d, device=device, generator=g).to(torch.bfloat16)
+    return kp, vp, tables
+
+
+def _history(pool, tables, i, L):
+    """Sequence i's (L, Hkv, d) history read from the pool with torch indexing (fp32, host)."""
+    import torch
+
+    bs = pool.shape[1]
+    blocks = torch.from_numpy(tables[i, : (L + bs - 1) // bs].astype(np.int64)).to(pool.device)
+    return pool.index_select(0, blocks).reshape(-1, *pool.shape[2:])[:L].float().cpu().numpy()
+
+
+def _check_sampled(out, q, kp, vp, tables, lens, pick, c, s, what):
+    for i in pick:
+        k, v = _history(kp, tables, i, lens[i]), _history(vp, tables, i, lens[i])
+        ref = oracle.decode_case_ref(q[i: i + 1], k.transpose(1, 0, 2)[None],
+                                     v.transpose(1, 0, 2)[None], c, s, causal=True)
+        assert_close_attn(out[i: i + 1], ref, what=f"{what} seq {i} (len {lens[i]})")
+
+
+@pytest.mark.parametrize("hkv,split", [(8, 0), (1, 0), (1, 512)],
+                         ids=["all_heads", "one_kv_head_slice", "one_kv_head_split512"])
+def test_config5_full_size_sampled(cuda, hkv, split):
+    """speculative verify, B=32, M=5, ctx ~ U[1024, 32768], d=128, block
+    size 16, random-permutation tables, at full size; checked on sampled sequences
+    (shortest, longest and three more) against the oracle. ``one_kv_head_slice`` is
+    what one rank of eight holds (Hq=4, Hkv=1): the automatic plan then makes more
+    partitions than the merge kernel's shared-memory path takes, so the partitions
+    are merged by its fallback path on full-length data (sequence 0 is given the
+    longest context the config allows, 32768, so that it has 33 partitions; with
+    512-token partitions every sequence has more than 32)."""
+    import torch
+    from kernels import _lib, build_rope_cache
+    from kernels.flash_attention import paged_attention
+
+    _lib.device_status(clear=True)
+    rng = np.random.default_rng(4)
+    ctx = rng.integers(1024, 32769, size=32)
+    ctx[0] = 32768
+    M, d, G = 5, 128, 4
+    lens = (ctx + M).tolist()
+    kp, vp, tables = _device_pool(lens, hkv, d, 16, 41 + hkv, cuda)
+    q = normal(400 + hkv, (32, G * hkv, M, d))
+    c, s = oracle.build_rope_cache(max(lens) + 1, d, 500000.0)
+    rope = build_rope_cache(max(lens) + 1, d, theta=500000.0, device=cuda)
+    out = to_np(paged_attention(to_torch(q, torch.bfloat16, cuda), kp, vp,
+                                torch.from_numpy(tables).to(cuda),
+                                torch.tensor(lens, dtype=torch.int32, device=cuda), True,
+                                rope=rope, split_tokens=split))
+    assert _lib.device_status(clear=True) == 0
+    assert np.isfinite(out).all()
+    pick = sorted({0, 31, int(np.argmax(lens)), int(np.argmin(lens)), 17})
+    _check_sampled(out, q, kp, vp, tables, lens, pick, c, s, f"cfg5 Hkv={hkv}")
