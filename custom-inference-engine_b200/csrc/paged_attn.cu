@@ -906,6 +906,16 @@ int dense_mma_attn(const void* q, const void* k, const void* v, void* o, int B, 
   return dispatch_d<false>(prm, d, pl.mt, bf16, st);
 }
 
+// Defined in prefill_attn.cu: the tcgen05 kernel reading the paged pools,
+// for query blocks of more than 64 rows per kv head (chunked prefill).
+bool paged_uses_tcgen05(int Hq, int Hkv, int M, int d, int block_size);
+int paged_prefill_tcgen05(const void* q, const void* k_pool, const void* v_pool,
+                          const int32_t* block_tables, const int32_t* kv_lens, void* o, int B,
+                          int Hq, int Hkv, int M, int d, int num_blocks, int block_size,
+                          int max_blocks, const int64_t* q_strides, const int64_t* o_strides,
+                          float scale, int causal, bool bf16, const float* rope_cos,
+                          const float* rope_sin, int rope_max_pos, cudaStream_t st);
+
 }  // namespace cie
 
 using namespace cie;
@@ -915,6 +925,7 @@ extern "C" size_t cie_paged_attn_workspace(int B, int Hq, int Hkv, int M, int d,
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || M <= 0 || Hq % Hkv != 0 || !mma_head_dim_ok(d) ||
       block_size <= 0 || max_blocks < 0)
     return 0;
+  if (paged_uses_tcgen05(Hq, Hkv, M, d, block_size)) return 0;
   return make_plan(B, Hq, Hkv, M, d, max_blocks * block_size, split_tokens).workspace();
 }
 
@@ -948,6 +959,13 @@ extern "C" int cie_paged_attn(const void* q, const void* k_pool, const void* v_p
     return CIE_ERR_UNSUPPORTED;
   }
   if (B == 0 || M == 0) return CIE_OK;
+  if (paged_uses_tcgen05(Hq, Hkv, M, d, block_size)) {
+    CIE_CHECK_ARG(B <= 65535, "cie_paged_attn: B must be <= 65535");
+    return paged_prefill_tcgen05(q, k_pool, v_pool, block_tables, kv_lens, o, B, Hq, Hkv, M, d,
+                                 num_blocks, block_size, max_blocks, q_strides, o_strides, scale,
+                                 causal, dtype == CIE_DTYPE_BF16, rope_cos, rope_sin,
+                                 rope_max_pos, reinterpret_cast<cudaStream_t>(stream));
+  }
   MmaPlan pl = make_plan(B, Hq, Hkv, M, d, max_blocks * block_size, split_tokens);
   if (pl.workspace() > 0 && (workspace == nullptr || workspace_bytes < pl.workspace())) {
     set_error("cie_paged_attn: workspace of %zu bytes required, got %zu", pl.workspace(),

@@ -32,6 +32,15 @@
 // TMA producers which K and V stages are free. Readiness of the next K and V
 // tiles is probed between MMAs, where the issuing thread stalls anyway.
 // Causal tile pairs are ordered heaviest first across the grid.
+//
+// Paged variant (PAGED = true): K and V are read straight from the engine's
+// paged pools (num_blocks, block_size, Hkv, d) through the block table, one
+// 16-token TMA box per table lookup (block_size a multiple of 16), and each
+// sequence b has its own history length kv_lens[b] (query i of the M new
+// tokens sits at position kv_lens[b] - M + i). This serves prefill of a batch
+// of sequences over non-empty histories (chunked prefill) in one launch, with
+// no dense gather. Boxes wholly past a sequence's length (or with a refused
+// block id) are fetched from outside the map and land as zeros.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -102,7 +111,27 @@ struct PrefillParams {
   const float* sin;
   int rope_max_pos;
   int rope_q_pos0;
+  // paged variant
+  const int32_t* kv_lens;   // (B,) history lengths including the M new tokens
+  const int32_t* tables;    // (B, max_blocks) physical block ids
+  int max_blocks, block_size, num_blocks;
+  int pool_tokens;          // num_blocks * block_size: the map's token extent
 };
+
+// Token coordinate of the 16-token box starting at logical position t of
+// sequence b in the paged pool map; past the sequence (or for a refused block
+// id) a coordinate outside the map, which TMA fills with zeros.
+__device__ __forceinline__ int paged_box_coord(const PrefillParams& p, const int32_t* table,
+                                               int t, int len) {
+  if (t >= len) return p.pool_tokens;
+  const int lb = t / p.block_size;
+  const int blk = lb < p.max_blocks ? table[lb] : -1;
+  if (blk < 0 || blk >= p.num_blocks) {
+    raise_status(CIE_DEV_BAD_BLOCK_ID);
+    return p.pool_tokens;
+  }
+  return blk * p.block_size + (t % p.block_size);
+}
 
 template <int D, bool BF16>
 __device__ __forceinline__ void rope_q_row(uint8_t* sQt, int row, int pos, const float* cos,
@@ -145,7 +174,7 @@ __device__ __forceinline__ void rope_q_row(uint8_t* sQt, int row, int pos, const
   }
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool PAGED>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
@@ -186,11 +215,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int h = bh % p.Hq;
   const int kvh = h / p.G;
   const int m0 = pr * 2 * kBM;
+  // history length of this sequence (the same for every b when dense)
+  int seq_n = p.N;
+  const int32_t* table = nullptr;
+  if constexpr (PAGED) {
+    seq_n = p.kv_lens[b];
+    const int cap = p.max_blocks * p.block_size;
+    if (seq_n < 0) seq_n = 0;
+    if (seq_n > cap) {
+      raise_status(CIE_DEV_BAD_BLOCK_ID);
+      seq_n = cap;
+    }
+    table = p.tables + static_cast<int64_t>(b) * p.max_blocks;
+  }
+  const int N = seq_n;
   int n_kv[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     const int mt0 = m0 + t * kBM;
-    int n_end = p.causal ? min(p.N, p.N - p.M + mt0 + kBM) : p.N;
+    int n_end = p.causal ? min(N, N - p.M + mt0 + kBM) : N;
     if (n_end < 0) n_end = 0;
     n_kv[t] = (mt0 < p.M) ? (n_end + kBN - 1) / kBN : 0;
   }
@@ -246,10 +289,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                           &g_wait_limit_ns))
           break;
         mbar_arrive_expect_tx(bar_k_full + st, C::KV_BYTES);
+        if constexpr (PAGED) {
+          int tok[kBN / 16];
 #pragma unroll
-        for (int c = 0; c < C::KCH; ++c)
-          tma_load_4d(sK + st * C::KV_BYTES + c * kBN * 128, &tm_k, bar_k_full + st, c * 64,
-                      j * kBN, kvh, b);
+          for (int i = 0; i < kBN / 16; ++i) tok[i] = paged_box_coord(p, table, j * kBN + i * 16, N);
+#pragma unroll
+          for (int c = 0; c < C::KCH; ++c)
+#pragma unroll
+            for (int i = 0; i < kBN / 16; ++i)
+              tma_load_4d(sK + st * C::KV_BYTES + c * kBN * 128 + i * 16 * 128, &tm_k,
+                          bar_k_full + st, c * 64, kvh, tok[i], 0);
+        } else {
+#pragma unroll
+          for (int c = 0; c < C::KCH; ++c)
+            tma_load_4d(sK + st * C::KV_BYTES + c * kBN * 128, &tm_k, bar_k_full + st, c * 64,
+                        j * kBN, kvh, b);
+        }
         issued = j + 1;
       }
       if (*abort_flag) {
@@ -273,10 +328,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                              &g_wait_limit_ns))
           break;
         mbar_arrive_expect_tx(bar_v_full + st, C::KV_BYTES);
+        if constexpr (PAGED) {
+          int tok[kBN / 16];
 #pragma unroll
-        for (int c = 0; c < C::KCH; ++c)
-          tma_load_4d(sV + st * C::KV_BYTES + c * kBN * 128, &tm_v, bar_v_full + st, c * 64,
-                      j * kBN, kvh, b);
+          for (int i = 0; i < kBN / 16; ++i) tok[i] = paged_box_coord(p, table, j * kBN + i * 16, N);
+#pragma unroll
+          for (int c = 0; c < C::KCH; ++c)
+#pragma unroll
+            for (int i = 0; i < kBN / 16; ++i)
+              tma_load_4d(sV + st * C::KV_BYTES + c * kBN * 128 + i * 16 * 128, &tm_v,
+                          bar_v_full + st, c * 64, kvh, tok[i], 0);
+        } else {
+#pragma unroll
+          for (int c = 0; c < C::KCH; ++c)
+            tma_load_4d(sV + st * C::KV_BYTES + c * kBN * 128, &tm_v, bar_v_full + st, c * 64,
+                        j * kBN, kvh, b);
+        }
         issued = j + 1;
       }
       if (*abort_flag) {
@@ -414,7 +481,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       ok = mbar_wait_bounded(bar_q_full, 0, abort_flag, &g_wait_limit_ns);
       ok = __all_sync(0xffffffffu, ok);
       if (ok && p.cos != nullptr && gm < p.M) {
-        int pos = p.rope_q_pos0 + gm;
+        int pos = (PAGED ? N - p.M : p.rope_q_pos0) + gm;
         if (pos < 0 || pos >= p.rope_max_pos) {
           raise_status(CIE_DEV_BAD_POSITION);
           pos = pos < 0 ? 0 : p.rope_max_pos - 1;
@@ -430,14 +497,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // no visible keys: N == 0 -> zeros (matches the fp32 reference), else NaN rows
       if (gm < p.M) {
         elem_t* o = reinterpret_cast<elem_t*>(p.o) + b * p.o_sb + h * p.o_sh + gm * p.o_sm;
-        const float fill = (p.N == 0) ? 0.f : __int_as_float(0x7fc00000);
+        const float fill = (N == 0) ? 0.f : __int_as_float(0x7fc00000);
         for (int d = 0; d < D; ++d) {
           if constexpr (BF16) o[d] = __float2bfloat16_rn(fill);
           else o[d] = __float2half_rn(fill);
         }
       }
     } else if (ok) {
-      const int lim = p.causal ? (p.N - p.M + gm) : (p.N - 1);  // keys <= lim are visible
+      const int lim = p.causal ? (N - p.M + gm) : (N - 1);  // keys <= lim are visible
       float m_run = -INFINITY;  // running max, log2 domain, scaled
       float l_run = 0.f;
       float sv[kBN];
@@ -629,11 +696,11 @@ static int make_map(CUtensorMap* map, const void* base, int d, int seq, int head
   return CIE_OK;
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool PAGED = false>
 static int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                           const PrefillParams& prm, cudaStream_t st) {
   constexpr int smem = PfCfg<D>::SMEM;
-  auto kern = prefill_attn_kernel<D, BF16>;
+  auto kern = prefill_attn_kernel<D, BF16, PAGED>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int grid = prm.n_pairs * prm.B * prm.Hq;
   kern<<<grid, kPfThreads, smem, st>>>(mq, mk, mv, prm);
@@ -656,6 +723,70 @@ int dense_mma_attn(const void* q, const void* k, const void* v, void* o, int B, 
 // and other head dims go to the split-KV mma.sync kernel over dense K/V.
 static bool use_tcgen05(int Hq, int Hkv, int M, int d) {
   return (d == 64 || d == 128) && static_cast<int64_t>(Hq / Hkv) * M > 64;
+}
+
+// Paged prefill on the tcgen05 kernel: q (B, Hq, M, d) dense, K/V from the
+// paged pools through the block table. Called by cie_paged_attn when the query
+// block is long enough for the tensor-core kernel (paged_uses_tcgen05).
+bool paged_uses_tcgen05(int Hq, int Hkv, int M, int d, int block_size) {
+  return use_tcgen05(Hq, Hkv, M, d) && block_size % 16 == 0;
+}
+
+int paged_prefill_tcgen05(const void* q, const void* k_pool, const void* v_pool,
+                          const int32_t* block_tables, const int32_t* kv_lens, void* o, int B,
+                          int Hq, int Hkv, int M, int d, int num_blocks, int block_size,
+                          int max_blocks, const int64_t* q_strides, const int64_t* o_strides,
+                          float scale, int causal, bool bf16, const float* rope_cos,
+                          const float* rope_sin, int rope_max_pos, cudaStream_t st) {
+  CIE_CHECK_ARG(aligned16(o) && o_strides[0] % 8 == 0 && o_strides[1] % 8 == 0 &&
+                    o_strides[2] % 8 == 0,
+                "cie_paged_attn: o must be 16-byte aligned with strides multiple of 8");
+  CIE_CHECK_ARG(rope_cos == nullptr || (aligned16(rope_cos) && aligned16(rope_sin)),
+                "cie_paged_attn: rope tables must be 16-byte aligned");
+  const int64_t pool_tokens = static_cast<int64_t>(num_blocks) * block_size;
+  CIE_CHECK_ARG(pool_tokens < (int64_t(1) << 31) - 16, "cie_paged_attn: pool too large");
+  PrefillParams prm{};
+  prm.B = B;
+  prm.Hq = Hq;
+  prm.Hkv = Hkv;
+  prm.M = M;
+  prm.N = 0;
+  prm.G = Hq / Hkv;
+  prm.n_pairs = (M + 2 * kBM - 1) / (2 * kBM);
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.causal = causal ? 1 : 0;
+  prm.o = o;
+  prm.o_sb = o_strides[0];
+  prm.o_sh = o_strides[1];
+  prm.o_sm = o_strides[2];
+  prm.cos = rope_cos;
+  prm.sin = rope_sin;
+  prm.rope_max_pos = rope_max_pos;
+  prm.kv_lens = kv_lens;
+  prm.tables = block_tables;
+  prm.max_blocks = max_blocks;
+  prm.block_size = block_size;
+  prm.num_blocks = num_blocks;
+  prm.pool_tokens = static_cast<int>(pool_tokens);
+  CUtensorMap mq, mk, mv;
+  int rc = make_map(&mq, q, d, M, Hq, B, q_strides, bf16, "cie_paged_attn(q)");
+  if (rc != CIE_OK) return rc;
+  // (d, head, pool token, 1) with a (64, 1, 16, 1) box: one 16-token slice of
+  // one head per table lookup, 128-byte swizzle as the dense tiles
+  const cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)Hkv, (cuuint64_t)pool_tokens, 1};
+  const cuuint64_t strides[3] = {(cuuint64_t)d * 2, (cuuint64_t)Hkv * d * 2,
+                                 (cuuint64_t)pool_tokens * Hkv * d * 2};
+  const cuuint32_t box[4] = {64, 1, 16, 1};
+  if (!make_kv_map(&mk, k_pool, d, dims, strides, box, bf16) ||
+      !make_kv_map(&mv, v_pool, d, dims, strides, box, bf16)) {
+    set_error("cie_paged_attn: cuTensorMapEncodeTiled failed for the pools");
+    return CIE_ERR_LAUNCH;
+  }
+  if (d == 64)
+    return bf16 ? launch_prefill<64, true, true>(mq, mk, mv, prm, st)
+                : launch_prefill<64, false, true>(mq, mk, mv, prm, st);
+  return bf16 ? launch_prefill<128, true, true>(mq, mk, mv, prm, st)
+              : launch_prefill<128, false, true>(mq, mk, mv, prm, st);
 }
 
 static size_t rope_k_bytes(int B, int Hkv, int N, int d) {

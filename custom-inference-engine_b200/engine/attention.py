@@ -37,6 +37,12 @@ from engine.cache.kv_cache import PagedKVCache
 PAGED_MAX_ROWS = 64
 
 
+def _paged_long_ok(cache: PagedKVCache, d: int) -> bool:
+    """Long query blocks over a history read the pools through the block table on
+    the tcgen05 kernel when its 16-token boxes fit the cache geometry."""
+    return cache.cfg.block_size % 16 == 0 and d in (64, 128)
+
+
 def flash_attention(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -100,6 +106,11 @@ def attention_forward(
     if N == L:
         # whole sequence in this call: attend over the new tokens directly
         return _fa(q, k, v, True, scale, rope=rope, rope_q_pos0=start, rope_k=True)
+    if _paged_long_ok(cache, d):
+        # chunked prefill: the tcgen05 kernel reads the history through the table
+        tab, lens = cache.device_tables([table])
+        return paged_attention(q, cache.k[layer_idx], cache.v[layer_idx], tab, lens, True,
+                               scale, rope=rope)
     hk, hv = cache.gather(layer_idx, table)  # rotated K as stored
     return _fa(q, hk.transpose(0, 1).unsqueeze(0), hv.transpose(0, 1).unsqueeze(0), True, scale,
                rope=rope, rope_q_pos0=start, rope_k=False)
@@ -159,8 +170,10 @@ def attention_forward_batch(
     step.starts[b] + i. One fused RoPE + paged append writes every sequence's K/V;
     decode / verify blocks (Hq/Hkv * L <= 64 rows per kv head) then take one
     split-KV paged attention launch over the whole batch. Longer blocks go to the
-    tcgen05 prefill kernel: in one launch when every history is empty, else per
-    sequence over its gathered history. Returns (B, Hq, L, d).
+    tcgen05 prefill kernel in one launch too: over the new tokens when every
+    history is empty, else reading each sequence's history through the block
+    table (block sizes that are multiples of 16, d 64 / 128; other geometries
+    gather each history and launch per sequence). Returns (B, Hq, L, d).
     """
     from kernels.flash_attention import flash_attention as _fa
     from kernels.flash_attention import paged_attention, rope_append
@@ -181,6 +194,9 @@ def attention_forward_batch(
                                step.kv_lens, True, scale, rope=rope)
     if all(s == 0 for s in step.starts):
         return _fa(q, k, v, True, scale, rope=rope, rope_q_pos0=0, rope_k=True)
+    if _paged_long_ok(cache, d):
+        return paged_attention(q, cache.k[layer_idx], cache.v[layer_idx], step.block_tables,
+                               step.kv_lens, True, scale, rope=rope)
     outs = []
     for b, table in enumerate(step.tables):
         hk, hv = cache.gather(layer_idx, table)

@@ -169,6 +169,11 @@ def paged_attention(
 ) -> torch.Tensor:
     """Attention of q against each sequence's paged K/V history.
 
+    Decode (M = 1) and verify (M = gamma + 1) run on the split-KV kernel; query
+    blocks of more than 64 rows per kv head (chunked prefill of a batch) run on
+    the tcgen05 prefill kernel, which reads the pools through the block table
+    (block sizes multiple of 16, D 64 / 128; ``split_tokens`` does not apply).
+
     q: (B, Hq, M, D); k_pool/v_pool: (num_blocks, block_size, Hkv, D) contiguous;
     block_tables: int32 (B, max_blocks) of physical block ids in logical order;
     kv_lens: int32 (B,) history length including the M query tokens, so query i

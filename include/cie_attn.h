@@ -102,6 +102,13 @@ size_t cie_prefill_attn_workspace(int B, int Hq, int Hkv, int M, int N, int d,
  *                 kv_lens[b] - M + i (K is stored pre-rotated in the pool).
  *   split_tokens: 0 = automatic; else tokens per split-KV partition (multiple
  *                 of 16). Partitions are merged by a log-sum-exp kernel.
+ * Query blocks of more than 64 rows per kv head ((Hq / Hkv) * M > 64, i.e.
+ * chunked prefill of a batch over non-empty histories) with d 64 or 128 and a
+ * block size that is a multiple of 16 run on the tcgen05 prefill kernel
+ * instead, which reads the pools through the table in 16-token TMA boxes (no
+ * gather, no workspace, split_tokens ignored); o must then be 16-byte aligned
+ * with strides multiples of 8 elements. This replaces the gather + dense
+ * attention of a chunked prefill (engine/model/block.py:65-71 with L > 1).
  */
 int cie_paged_attn(const void* q, const void* k_pool, const void* v_pool,
                    const int32_t* block_tables, const int32_t* kv_lens,

@@ -275,3 +275,62 @@ def test_batched_step_matches_per_sequence(cuda, d):
         ka, va = ca.gather(0, ta[b])
         kb, vb = cb.gather(0, tb[b])
         assert torch.equal(ka, kb) and torch.equal(va, vb)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_batched_step_vs_oracle(cuda, d):
+    """The batched engine step against the oracle (not just against the CUDA
+    per-sequence path): ragged histories (0, 40 and 171 tokens), then batch steps
+    of decode (L=1), speculative verify (L=5), a chunked-prefill block (L=100,
+    one tcgen05 launch reading the pools through the table) and decode again.
+    The oracle keeps the raw K/V of every token, rotates K at its position (the
+    cache stores rotated K, bf16-rounded, which the kernels reproduce bit for bit)
+    and attends bottom-right causally with q rotated at its positions."""
+    import torch
+
+    import oracle
+    from engine.attention import attention_forward, attention_forward_batch, begin_step
+    from kernels import build_rope_cache
+    from tests.golden.inputs import normal
+
+    hq, hkv, B = 8, 2, 3
+    c, s = oracle.build_rope_cache(2048, d, 500000.0)
+    rope = build_rope_cache(2048, d, theta=500000.0, device=cuda)
+    cache = _cache(1, hkv, d, cuda, blocks=160, bs=16)
+    tables = [cache.new_sequence() for _ in range(B)]
+    hist_k = [np.zeros((hkv, 0, d), np.float32) for _ in range(B)]
+    hist_v = [np.zeros((hkv, 0, d), np.float32) for _ in range(B)]
+    seed = [d * 100]
+
+    def draw(shape):
+        seed[0] += 1
+        return normal(seed[0], shape)
+
+    def remember(b, k, v, start):
+        L = k.shape[1]
+        krot = oracle.bf16_round(oracle.apply_rotary(k[None], c, s, np.arange(start, start + L))[0])
+        hist_k[b] = np.concatenate([hist_k[b], krot], axis=1)
+        hist_v[b] = np.concatenate([hist_v[b], v], axis=1)
+
+    for b, n in enumerate((0, 40, 171)):
+        if n:
+            q, k, v = draw((1, hq, n, d)), draw((1, hkv, n, d)), draw((1, hkv, n, d))
+            attention_forward(*(to_t(x, cuda) for x in (q, k, v)), cache, 0, tables[b], rope=rope)
+            remember(b, k[0], v[0], 0)
+    for L in (1, 5, 100, 1):
+        q, k, v = draw((B, hq, L, d)), draw((B, hkv, L, d)), draw((B, hkv, L, d))
+        step = begin_step(cache, tables, L)
+        out = attention_forward_batch(*(to_t(x, cuda) for x in (q, k, v)), cache, 0, step,
+                                      rope=rope).float().cpu().numpy()
+        for b in range(B):
+            start = step.starts[b]
+            remember(b, k[b], v[b], start)
+            qr = oracle.apply_rotary(q[b:b + 1], c, s, np.arange(start, start + L))
+            ref = oracle.attention(qr, hist_k[b][None], hist_v[b][None], causal=True)
+            assert_close_attn(out[b:b + 1], ref, what=f"L={L} seq {b} (history {start})")
+
+
+def to_t(x, device):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(x)).to(device=device, dtype=torch.bfloat16)

@@ -267,3 +267,57 @@ def test_config5_full_size_sampled(cuda, hkv, split):
     assert np.isfinite(out).all()
     pick = sorted({0, 31, int(np.argmax(lens)), int(np.argmin(lens)), 17})
     _check_sampled(out, q, kp, vp, tables, lens, pick, c, s, f"cfg5 Hkv={hkv}")
+
+
+PAGED_PREFILL_CASES = [
+    # B, Hq, Hkv, M, d, bs, kv_lens (history incl. the M new tokens)
+    (3, 8, 2, 100, 64, 16, [100, 137, 1100]),
+    (2, 8, 2, 300, 128, 16, [300, 2000]),
+    (3, 16, 2, 77, 128, 32, [77, 500, 1029]),
+    (1, 32, 8, 513, 64, 16, [4000]),
+    (2, 4, 1, 129, 128, 64, [129, 1000]),
+]
+
+
+@pytest.mark.parametrize("case", PAGED_PREFILL_CASES,
+                         ids=lambda c: f"B{c[0]}H{c[1]}-{c[2]}M{c[3]}d{c[4]}bs{c[5]}")
+@pytest.mark.parametrize("dt", ["bf16", "fp16"])
+def test_paged_prefill_vs_oracle(cuda, case, dt):
+    """Chunked prefill of a batch: M new tokens per sequence (G*M > 64 rows per kv
+    head) against ragged paged histories, on the tcgen05 kernel reading the pools
+    through the block table; q rotated at positions kv_len - M + i."""
+    import torch
+    from kernels import build_rope_cache
+    from kernels.flash_attention import paged_attention
+
+    B, Hq, Hkv, M, d, bs, lens = case
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float16
+    seed = (B * 31 + Hq * 7 + M + d + bs) % 9973
+    c, s = oracle.build_rope_cache(max(lens) + 4, d, 500000.0)
+    kp, vp, tables, ks, vs = build_paged(lens, Hkv, d, bs, seed, c, s)
+    q = normal(seed + 7, (B, Hq, M, d))
+    rope = build_rope_cache(max(lens) + 4, d, theta=500000.0, device=cuda)
+    out = paged_attention(to_torch(q, tdt, cuda), to_torch(kp, tdt, cuda), to_torch(vp, tdt, cuda),
+                          torch.from_numpy(tables).to(cuda),
+                          torch.tensor(lens, dtype=torch.int32, device=cuda), True, rope=rope)
+    assert_close_attn(to_np(out), ref_paged(q, ks, vs, lens, c, s), what=str(case))
+
+
+def test_paged_prefill_bad_block_id_sets_status(cuda):
+    """A refused block id in the tcgen05 paged path: status bit, zeros fetched,
+    finite output, and the context stays usable."""
+    import torch
+    from kernels import _lib
+    from kernels.flash_attention import paged_attention
+
+    _lib.device_status(clear=True)
+    lens = [400]
+    kp, vp, tables, ks, vs = build_paged(lens, 2, 64, 16, 19)
+    tables[0, 3] = kp.shape[0] + 7
+    q = to_torch(normal(20, (1, 8, 200, 64)), torch.bfloat16, cuda)
+    out = paged_attention(q, to_torch(kp, torch.bfloat16, cuda), to_torch(vp, torch.bfloat16, cuda),
+                          torch.from_numpy(tables).cuda(), torch.tensor(lens, dtype=torch.int32).cuda())
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) & _lib.CIE_DEV_BAD_BLOCK_ID
+    assert torch.isfinite(out).all()
+    assert _lib.device_status(clear=True) == 0
