@@ -219,7 +219,7 @@ def l2_flush_buffer():
 class PrefillWorkload:
     """One rank's slice of a causal RoPE prefill (kv-head group sharding)."""
 
-    def __init__(self, cfg, world, rank, seed=0, chunks=1):
+    def __init__(self, cfg, world, rank, seed=0, chunks=1, gather="peers"):
         import torch
 
         from engine.head_shard import local_heads, shard_heads
@@ -242,6 +242,19 @@ class PrefillWorkload:
         self.chunks = chunks if world > 1 else 1
         if self.chunks < 1 or B % self.chunks:
             raise ValueError(f"--chunks {self.chunks} must divide the batch ({B})")
+        # N > 1: the fused kernel writes every output tile into every rank's full
+        # output over NVLink (symmetric memory); NCCL all-gather if that cannot be set up
+        self.peer, self.gather = None, "none (1 GPU)"
+        if world > 1:
+            self.gather = "nccl all_gather_into_tensor, batch chunks"
+            if gather == "peers":
+                from engine.head_shard import PeerOutput
+
+                try:
+                    self.peer = PeerOutput((B, cfg["Hq"], S, d), torch.bfloat16, "cuda")
+                    self.gather = "fused: output tiles stored to peers inside the kernel + peer barrier"
+                except Exception as e:  # noqa: BLE001 - reported in the JSON line
+                    self.gather = f"nccl (symmetric memory unavailable: {type(e).__name__}: {e})"
         self.flops_total = prefill_flops(B, cfg["Hq"], S, d)
         self.launches_per_step = 2  # rope(K) + attention
         self.kernel_ms = []
@@ -264,6 +277,8 @@ class PrefillWorkload:
 
         if self.world == 1:
             return torch.cat(outs, 0)
+        if self.peer is not None:
+            return outs[0]                         # already (B, Hq, S, d) on every rank
         g = torch.cat(outs, 1)                     # (W, B, hq, S, d), rank-major
         W, B, hq, S, d = g.shape
         return g.permute(1, 0, 2, 3, 4).reshape(B, W * hq, S, d)
@@ -301,6 +316,12 @@ class PrefillWorkload:
         k_rot = apply_rotary(self.k, self.cos, self.sin)
         if events is not None:
             events[0].record()
+        if self.peer is not None:
+            full = self.peer.attention(self.q, k_rot, self.v, self.shard, True, self.scale,
+                                       rope=(self.cos, self.sin), rope_k=False,
+                                       on_kernel_done=(events[1].record if events is not None
+                                                       else None))
+            return [full]
         B = self.cfg["B"]
         per = B // self.chunks
         works, outs = [], []
@@ -816,6 +837,9 @@ def main():
     ap.add_argument("--chunks", type=int, default=0,
                     help="N > 1: batch chunks whose all-gather overlaps the next chunk's "
                          "attention (0: the measured default)")
+    ap.add_argument("--gather", choices=["peers", "nccl"], default="peers",
+                    help="N > 1: output all-gather fused into the kernel over peer memory "
+                         "(default) or NCCL all_gather_into_tensor")
     ap.add_argument("--batch", type=int, default=0,
                     help="with --only: override the batch size (smaller ncu captures)")
     ap.add_argument("--cpu-worker", default="", help=argparse.SUPPRESS)
@@ -847,7 +871,8 @@ def main():
     # ---------------- headline
     # measured: 4 chunks best at N <= 4 (the gather hides behind later chunks), 1 at N = 8
     # (the gather dominates and smaller launches only lose waves)
-    wl = PrefillWorkload(HEADLINE, world, rank, chunks=args.chunks or (4 if world <= 4 else 1))
+    wl = PrefillWorkload(HEADLINE, world, rank, chunks=args.chunks or (4 if world <= 4 else 1),
+                         gather=args.gather)
     clocks = ClockSampler()
     if rank == 0:
         clocks.start()
@@ -865,7 +890,8 @@ def main():
             "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
             "traffic": traffic if world == 1 else None,
             "kernel": "prefill_attn_kernel<128,bf16> (tcgen05)", "kernel_ms": kern_ms}
-    launches = args.steps * (1 + wl.chunks)
+    launches = args.steps * ((3 if wl.peer is not None else 1 + wl.chunks) if world > 1 else 2)
+    gather_mode = wl.gather
     check = wl.check_against_one_gpu() if world > 1 else None
     del wl
     torch.cuda.empty_cache()
@@ -952,7 +978,7 @@ def main():
             "config": {"workload": HEADLINE["name"] + ": causal GQA prefill + fused RoPE",
                        "B": HEADLINE["B"], "S": HEADLINE["S"], "Hq": HEADLINE["Hq"],
                        "Hkv": HEADLINE["Hkv"], "d": HEADLINE["d"],
-                       "parallelism": f"kv-head groups / {world} + NCCL all-gather"
+                       "parallelism": f"kv-head groups / {world}; output gather: {gather_mode}"
                        if world > 1 else "1 GPU",
                        "l2": "inputs larger than L2 (402 MB per step)"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,

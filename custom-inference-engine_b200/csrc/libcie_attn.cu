@@ -7,3 +7,4 @@
 #include "paged_noalloc.cu"
 #include "prefill_attn.cu"
 #include "int8_gemm.cu"
+#include "peer_barrier.cu"

@@ -58,7 +58,7 @@ constexpr int kPfThreads = 384;  // 3 warpgroups
 // warpgroups. The split (ctrl + 2 * softmax <= 3 * 168) is the one ptxas
 // compiles without spills for each head dim.
 template <int D>
-constexpr int kRegsCtrl = D >= 128 ? 80 : 64;
+constexpr int kRegsCtrl = D >= 128 ? 88 : 72;
 template <int D>
 constexpr int kRegsSoftmax = D >= 128 ? 208 : 216;
 #ifndef CIE_KSTAGES_D128
@@ -76,6 +76,7 @@ constexpr int kRegsSoftmax = D >= 128 ? 208 : 216;
 #ifndef CIE_MAX_CHAINS
 #define CIE_MAX_CHAINS 8
 #endif
+constexpr int kMaxPeers = 7;     // other GPUs an output tile can be copied to
 constexpr int kBM = 128;         // rows of one query tile; a CTA owns two
 constexpr int kBN = 128;         // keys per K/V tile
 
@@ -93,7 +94,7 @@ struct PfCfg {
   static constexpr int R = 8;
   static_assert(R > KS && R > VS, "step ring must be deeper than the K/V rings");
   static constexpr int BAR_OFF = 2 * Q_BYTES + (KS + VS) * KV_BYTES;
-  static constexpr int NBARS = 2 + KS + VS + 1 + R + 2 + 2 + 2 + 1;
+  static constexpr int NBARS = 3 + KS + VS + 1 + R + 2 + 2 + 2 + 2 + 1;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 /*tmem slot, abort*/ + 1024 /*align*/;
   static constexpr uint32_t TM_S0 = 0, TM_S1 = 128;    // P_t aliases cols [0, 64) of S_t
   static constexpr uint32_t TM_O0 = 256, TM_O1 = 256 + D;
@@ -103,6 +104,7 @@ struct PfCfg {
 struct PrefillParams {
   int B, Hq, Hkv, M, N, G;
   int n_pairs;  // query tile pairs per (batch, head)
+  int n_units;  // n_pairs * B * Hq: the work list the persistent grid walks
   float scale_log2;
   int causal;
   void* o;
@@ -116,6 +118,10 @@ struct PrefillParams {
   const int32_t* tables;    // (B, max_blocks) physical block ids
   int max_blocks, block_size, num_blocks;
   int pool_tokens;          // num_blocks * block_size: the map's token extent
+  // output all-gather over peer memory: the same rows also go to n_peers other
+  // GPUs' outputs (same layout as o, pointers already at this rank's heads)
+  void* o_peers[kMaxPeers];
+  int n_peers;
 };
 
 // Token coordinate of the 16-token box starting at logical position t of
@@ -174,6 +180,60 @@ __device__ __forceinline__ void rope_q_row(uint8_t* sQt, int row, int pos, const
   }
 }
 
+// One work unit: two 128-row query tiles (rows m0 .. m0 + 255) of one (batch,
+// head) and the key tiles they see.
+struct PfUnit {
+  int b, h, kvh, m0, N;
+  int n_kv[2];  // key tiles of query tile 0 / 1
+  int n;        // max of the two: key steps of the unit
+  const int32_t* table;
+};
+
+// Unit u of the grid's work list, heaviest first when causal (the causal work
+// of a tile pair grows with its position).
+template <bool PAGED>
+__device__ __forceinline__ PfUnit pf_unit(const PrefillParams& p, int u) {
+  PfUnit w;
+  const int bh_count = p.B * p.Hq;
+  const int pair_lin = u / bh_count;
+  const int pr = p.causal ? (p.n_pairs - 1 - pair_lin) : pair_lin;
+  const int bh = u % bh_count;
+  w.b = bh / p.Hq;
+  w.h = bh % p.Hq;
+  w.kvh = w.h / p.G;
+  w.m0 = pr * 2 * kBM;
+  w.N = p.N;
+  w.table = nullptr;
+  if constexpr (PAGED) {
+    int n = p.kv_lens[w.b];
+    const int cap = p.max_blocks * p.block_size;
+    if (n < 0) n = 0;
+    if (n > cap) n = cap;  // the bad length is reported once, by softmax thread 0
+    w.N = n;
+    w.table = p.tables + static_cast<int64_t>(w.b) * p.max_blocks;
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int mt0 = w.m0 + t * kBM;
+    int n_end = p.causal ? min(w.N, w.N - p.M + mt0 + kBM) : w.N;
+    if (n_end < 0) n_end = 0;
+    w.n_kv[t] = (mt0 < p.M) ? (n_end + kBN - 1) / kBN : 0;
+  }
+  w.n = max(w.n_kv[0], w.n_kv[1]);
+  return w;
+}
+
+// The CTA's units: round r takes unit r * G + c, and r * G + (G - 1 - c) on odd
+// rounds (a snake over the heaviest-first list, so every CTA gets a similar mix
+// of heavy and light units). -2: no more rounds; -1: nothing in this round.
+__device__ __forceinline__ int pf_unit_index(int r, int n_units) {
+  const int G = gridDim.x, c = blockIdx.x;
+  const int base = r * G;
+  if (base >= n_units) return -2;
+  const int u = base + ((r & 1) ? (G - 1 - c) : c);
+  return u < n_units ? u : -1;
+}
+
 template <int D, bool BF16, bool PAGED>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -183,65 +243,37 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                          // [2][KCH][128][128B]
-  uint8_t* sK = sQ + 2 * C::Q_BYTES;      // [KS][KCH][128][128B]
+  uint8_t* sQ = smem;                      // [2][KCH][128][128B]
+  uint8_t* sK = sQ + 2 * C::Q_BYTES;       // [KS][KCH][128][128B]
   uint8_t* sV = sK + C::KS * C::KV_BYTES;  // [VS][KCH][128][128B]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-  uint64_t* bar_q_full = bars + 0;
-  uint64_t* bar_q_ready = bars + 1;
-  uint64_t* bar_k_full = bars + 2;
+  uint64_t* bar_q_full = bars + 0;   // Q tiles of the unit landed
+  uint64_t* bar_q_ready = bars + 1;  // ... and rotated (three loader warps arrive)
+  uint64_t* bar_q_free = bars + 2;   // every S MMA of the unit complete: Q may be replaced
+  uint64_t* bar_k_full = bars + 3;
   uint64_t* bar_v_full = bar_k_full + C::KS;
-  uint64_t* bar_s0_full = bar_v_full + C::VS;  // S0_j complete (and PV0_{j-1})
-  // bar_step[i % R], phase i / R: every MMA up to S1_i complete. Frees K_i's
-  // stage (S0_i, S1_i done) and V_{i-1}'s stage (PV0_{i-1}, PV1_{i-1} done), and
-  // is softmax 1's "S1_i ready".
+  uint64_t* bar_s0_full = bar_v_full + C::VS;  // S0 of a key step complete (and PV0 before it)
+  // bar_step[g % R], phase g / R, for the CTA's g-th key step (counted over all
+  // its units): every MMA up to S1 of that step complete. Frees K_g's stage (S0_g,
+  // S1_g done) and V_{g-1}'s stage (PV0_{g-1}, PV1_{g-1} done), and is softmax 1's
+  // "S1 ready".
   uint64_t* bar_step = bar_s0_full + 1;
-  uint64_t* bar_pa_full = bar_step + C::R;  // [2] per tile: P_t keys 0..63 written
-  uint64_t* bar_p_full = bar_pa_full + 2;   // [2] per tile: all of P_t written
-  uint64_t* bar_o_final = bar_p_full + 2;   // [2] per tile
-  uint64_t* bar_drain = bar_o_final + 2;           // [1] abort path only
+  uint64_t* bar_pa_full = bar_step + C::R;  // [2] per tile: P keys 0..63 written
+  uint64_t* bar_p_full = bar_pa_full + 2;   // [2] per tile: all of P written
+  uint64_t* bar_o_final = bar_p_full + 2;   // [2] per tile: last PV of the unit complete
+  uint64_t* bar_o_stored = bar_o_final + 2; // [2] per tile: the unit's rows are in o
+  uint64_t* bar_drain = bar_o_stored + 2;   // [1] abort path only
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // heaviest tile pairs first when causal
-  const int bh_count = p.B * p.Hq;
-  const int pair_lin = blockIdx.x / bh_count;
-  const int pr = p.causal ? (p.n_pairs - 1 - pair_lin) : pair_lin;
-  const int bh = blockIdx.x % bh_count;
-  const int b = bh / p.Hq;
-  const int h = bh % p.Hq;
-  const int kvh = h / p.G;
-  const int m0 = pr * 2 * kBM;
-  // history length of this sequence (the same for every b when dense)
-  int seq_n = p.N;
-  const int32_t* table = nullptr;
-  if constexpr (PAGED) {
-    seq_n = p.kv_lens[b];
-    const int cap = p.max_blocks * p.block_size;
-    if (seq_n < 0) seq_n = 0;
-    if (seq_n > cap) {
-      raise_status(CIE_DEV_BAD_BLOCK_ID);
-      seq_n = cap;
-    }
-    table = p.tables + static_cast<int64_t>(b) * p.max_blocks;
-  }
-  const int N = seq_n;
-  int n_kv[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int mt0 = m0 + t * kBM;
-    int n_end = p.causal ? min(N, N - p.M + mt0 + kBM) : N;
-    if (n_end < 0) n_end = 0;
-    n_kv[t] = (mt0 < p.M) ? (n_end + kBN - 1) / kBN : 0;
-  }
-  const int n_kv_max = max(n_kv[0], n_kv[1]);
+  const int n_units = p.n_units;
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 1);
-    mbar_init(bar_q_ready, 8);  // one arrive per softmax warp
+    mbar_init(bar_q_ready, 2);
+    mbar_init(bar_q_free, 1);
     for (int s = 0; s < C::KS; ++s) mbar_init(bar_k_full + s, 1);
     for (int s = 0; s < C::VS; ++s) mbar_init(bar_v_full + s, 1);
     mbar_init(bar_s0_full, 1);
@@ -252,6 +284,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(bar_pa_full + t, 4);
       mbar_init(bar_p_full + t, 4);
       mbar_init(bar_o_final + t, 1);
+      mbar_init(bar_o_stored + t, 4);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -268,199 +301,331 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
   if (warp < 4) {
    reg_dealloc<kRegsCtrl<D>>();
-   if (warp == 0) {
-    // ------------------------------------------------ TMA producer: Q and K
-    if (lane == 0 && n_kv_max > 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      mbar_arrive_expect_tx(bar_q_full, 2 * C::Q_BYTES);
+   if (warp == 3) {
+    // -------------------------------------- output all-gather over peer memory
+    // Each unit's output rows, once the softmax warpgroups stored them to o,
+    // are copied to the other GPUs' outputs with 16-byte peer stores, while the
+    // CTA computes its next unit: the NVLink transfer overlaps the math unit by
+    // unit. Idle when there are no peers.
+    if (p.n_peers > 0) {
+      bool ok = true;
+      int ui = 0;  // units of this CTA so far (every unit, with keys or not)
+      using vec_t = uint4;
+      for (int r = 0; ok; ++r) {
+        const int u = pf_unit_index(r, n_units);
+        if (u == -2) break;
+        if (u < 0) continue;
+        const PfUnit w = pf_unit<PAGED>(p, u);
+        for (int t = 0; t < 2 && ok; ++t) {
+          ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_o_stored + t, ui & 1, abort_flag,
+                                                         &g_wait_limit_ns));
+          if (!ok) break;
+          const int mt0 = w.m0 + t * kBM;
+          const int rows = min(kBM, p.M - mt0);
+          if (rows <= 0) continue;
+          constexpr int CH = D * 2 / 16;  // 16-byte chunks per row
+          const int64_t base = static_cast<int64_t>(w.b) * p.o_sb + w.h * p.o_sh;
+          const uint8_t* src = reinterpret_cast<const uint8_t*>(p.o);
+          for (int q0 = lane; q0 < rows * CH; q0 += 32 * 4) {
+            vec_t v[4];
+            int64_t off[4];
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+            for (int i = 0; i < 4; ++i) {
+              const int q = q0 + 32 * i;
+              off[i] = -1;
+              if (q < rows * CH) {
+                off[i] = (base + static_cast<int64_t>(mt0 + q / CH) * p.o_sm) * 2 + (q % CH) * 16;
+                v[i] = *reinterpret_cast<const vec_t*>(src + off[i]);
+              }
+            }
+            for (int pe = 0; pe < p.n_peers; ++pe) {
+              uint8_t* dst = reinterpret_cast<uint8_t*>(p.o_peers[pe]);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                if (off[i] >= 0) *reinterpret_cast<vec_t*>(dst + off[i]) = v[i];
+            }
+          }
+        }
+        ++ui;
+      }
+      // make every peer store visible system-wide before the kernel ends; the
+      // barrier that follows the kernel then publishes them
+      __threadfence_system();
+    }
+   } else if (warp != 1) {
+    // -------------------------------------- loaders (warp 0: Q and K, warp 2: V)
+    // and RoPE of Q (warps 0 and 2 together). Lane 0 of each issues the TMA
+    // copies; at a unit boundary it first issues the copies whose stages earlier
+    // units free, then the two warps rotate the new Q tiles in shared memory,
+    // then it issues the rest (their stages are freed by this unit's MMAs, which
+    // wait for the rotated Q).
+    const bool kload = warp == 0, vload = warp == 2;
+    if (lane == 0) {
+      if (kload) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+      } else if (vload) {
+        tma_prefetch_desc(&tm_v);
+      }
+    }
+    int k_issued = 0, v_issued = 0, q_issued = 0;  // totals, for the drain on abort
+    // K tile g (the CTA's g-th key step) into its stage; j = tile within the unit
+    auto load_k = [&](int g, const PfUnit& w, int j) -> bool {
+      const int st = g % C::KS;
+      // K_{g-KS} left this stage once S1_{g-KS} completed
+      if (g >= C::KS && !mbar_wait_bounded(bar_step + (g - C::KS) % C::R,
+                                           ((g - C::KS) / C::R) & 1, abort_flag,
+                                           &g_wait_limit_ns))
+        return false;
+      mbar_arrive_expect_tx(bar_k_full + st, C::KV_BYTES);
+      if constexpr (PAGED) {
+        int tok[kBN / 16];
+#pragma unroll
+        for (int i = 0; i < kBN / 16; ++i) tok[i] = paged_box_coord(p, w.table, j * kBN + i * 16, w.N);
 #pragma unroll
         for (int c = 0; c < C::KCH; ++c)
-          tma_load_4d(sQ + t * C::Q_BYTES + c * kBM * 128, &tm_q, bar_q_full, c * 64,
-                      m0 + t * kBM, h, b);
-      int issued = 0;
-      for (int j = 0; j < n_kv_max; ++j) {
-        const int st = j % C::KS;
-        // K_{j-KS} left this stage once S1_{j-KS} completed
-        const int fr = j - C::KS;
-        if (fr >= 0 && !mbar_wait_bounded(bar_step + fr % C::R, (fr / C::R) & 1, abort_flag,
-                                          &g_wait_limit_ns))
-          break;
-        mbar_arrive_expect_tx(bar_k_full + st, C::KV_BYTES);
-        if constexpr (PAGED) {
-          int tok[kBN / 16];
 #pragma unroll
-          for (int i = 0; i < kBN / 16; ++i) tok[i] = paged_box_coord(p, table, j * kBN + i * 16, N);
+          for (int i = 0; i < kBN / 16; ++i)
+            tma_load_4d(sK + st * C::KV_BYTES + c * kBN * 128 + i * 16 * 128, &tm_k,
+                        bar_k_full + st, c * 64, w.kvh, tok[i], 0);
+      } else {
 #pragma unroll
-          for (int c = 0; c < C::KCH; ++c)
-#pragma unroll
-            for (int i = 0; i < kBN / 16; ++i)
-              tma_load_4d(sK + st * C::KV_BYTES + c * kBN * 128 + i * 16 * 128, &tm_k,
-                          bar_k_full + st, c * 64, kvh, tok[i], 0);
-        } else {
-#pragma unroll
-          for (int c = 0; c < C::KCH; ++c)
-            tma_load_4d(sK + st * C::KV_BYTES + c * kBN * 128, &tm_k, bar_k_full + st, c * 64,
-                        j * kBN, kvh, b);
-        }
-        issued = j + 1;
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(sK + st * C::KV_BYTES + c * kBN * 128, &tm_k, bar_k_full + st, c * 64,
+                      j * kBN, w.kvh, w.b);
       }
-      if (*abort_flag) {
-        // let this CTA's copies still in flight land before its smem is released:
-        // the newest load of each stage is the latest phase of that stage's barrier
-        mbar_wait_timeout(bar_q_full, 0, kWaitLimitNs);
-        for (int j = issued - 1; j >= 0 && j >= issued - C::KS; --j)
-          mbar_wait_timeout(bar_k_full + (j % C::KS), (j / C::KS) & 1, kWaitLimitNs);
+      k_issued = g + 1;
+      return true;
+    };
+    auto load_v = [&](int g, const PfUnit& w, int j) -> bool {
+      const int st = g % C::VS;
+      // V_{g-VS} left this stage once PV1_{g-VS} completed, i.e. by step g-VS+1
+      if (g >= C::VS && !mbar_wait_bounded(bar_step + (g - C::VS + 1) % C::R,
+                                           ((g - C::VS + 1) / C::R) & 1, abort_flag,
+                                           &g_wait_limit_ns))
+        return false;
+      mbar_arrive_expect_tx(bar_v_full + st, C::KV_BYTES);
+      if constexpr (PAGED) {
+        int tok[kBN / 16];
+#pragma unroll
+        for (int i = 0; i < kBN / 16; ++i) tok[i] = paged_box_coord(p, w.table, j * kBN + i * 16, w.N);
+#pragma unroll
+        for (int c = 0; c < C::KCH; ++c)
+#pragma unroll
+          for (int i = 0; i < kBN / 16; ++i)
+            tma_load_4d(sV + st * C::KV_BYTES + c * kBN * 128 + i * 16 * 128, &tm_v,
+                        bar_v_full + st, c * 64, w.kvh, tok[i], 0);
+      } else {
+#pragma unroll
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(sV + st * C::KV_BYTES + c * kBN * 128, &tm_v, bar_v_full + st, c * 64,
+                      j * kBN, w.kvh, w.b);
+      }
+      v_issued = g + 1;
+      return true;
+    };
+    const int rope_lane = (warp == 0 ? 0 : 32) + lane;
+    int kt = 0, qi = 0;  // key steps and units (with keys) before the current unit
+    bool ok = true;
+    for (int r = 0; ok; ++r) {
+      const int u = pf_unit_index(r, n_units);
+      if (u == -2) break;
+      if (u < 0) continue;
+      const PfUnit w = pf_unit<PAGED>(p, u);
+      if (w.n == 0) continue;
+      int kj = 0, vj = 0;  // next K / V tile of the unit
+      if (lane == 0) {
+        if (kload) {
+          // Q may be replaced once every S MMA of the previous unit completed
+          if (qi > 0)
+            ok = mbar_wait_bounded(bar_q_free, (qi - 1) & 1, abort_flag, &g_wait_limit_ns);
+          if (ok) {
+            mbar_arrive_expect_tx(bar_q_full, 2 * C::Q_BYTES);
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+              for (int c = 0; c < C::KCH; ++c)
+                tma_load_4d(sQ + t * C::Q_BYTES + c * kBM * 128, &tm_q, bar_q_full, c * 64,
+                            w.m0 + t * kBM, w.h, w.b);
+            q_issued = qi + 1;
+          }
+          // K stages freed by earlier units: tiles j < KS
+          for (; ok && kj < w.n && kj < C::KS; ++kj) ok = load_k(kt + kj, w, kj);
+        } else if (vload) {
+          for (; ok && vj < w.n && vj < C::VS - 1; ++vj) ok = load_v(kt + vj, w, vj);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (ok) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait_bounded(bar_q_full, qi & 1, abort_flag, &g_wait_limit_ns));
+      }
+      if (!ok) break;
+      if (p.cos != nullptr) {
+        const int pos0 = PAGED ? w.N - p.M : p.rope_q_pos0;
+        for (int rr = rope_lane; rr < 2 * kBM; rr += 64) {
+          const int t = rr / kBM, row = rr % kBM;
+          const int gm = w.m0 + t * kBM + row;
+          if (gm >= p.M) continue;
+          int pos = pos0 + gm;
+          if (pos < 0 || pos >= p.rope_max_pos) {
+            raise_status(CIE_DEV_BAD_POSITION);
+            pos = pos < 0 ? 0 : p.rope_max_pos - 1;
+          }
+          rope_q_row<D, BF16>(sQ + t * C::Q_BYTES, row, pos, p.cos, p.sin);
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(bar_q_ready);
+        if (kload) {
+          for (; ok && kj < w.n; ++kj) ok = load_k(kt + kj, w, kj);
+        } else if (vload) {
+          for (; ok && vj < w.n; ++vj) ok = load_v(kt + vj, w, vj);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      kt += w.n;
+      ++qi;
+    }
+    if (*abort_flag && lane == 0) {
+      // let this CTA's copies still in flight land before its smem is released:
+      // the newest load of each stage is the latest phase of that stage's barrier
+      if (kload) {
+        if (q_issued > 0) mbar_wait_timeout(bar_q_full, (q_issued - 1) & 1, kWaitLimitNs);
+        for (int g = k_issued - 1; g >= 0 && g >= k_issued - C::KS; --g)
+          mbar_wait_timeout(bar_k_full + (g % C::KS), (g / C::KS) & 1, kWaitLimitNs);
+      } else if (vload) {
+        for (int g = v_issued - 1; g >= 0 && g >= v_issued - C::VS; --g)
+          mbar_wait_timeout(bar_v_full + (g % C::VS), (g / C::VS) & 1, kWaitLimitNs);
       }
     }
-  } else if (warp == 2) {
-    // ------------------------------------------------ TMA producer: V
-    if (lane == 0 && n_kv_max > 0) {
-      tma_prefetch_desc(&tm_v);
-      int issued = 0;
-      for (int j = 0; j < n_kv_max; ++j) {
-        const int st = j % C::VS;
-        // V_{j-VS} left this stage once PV1_{j-VS} completed, i.e. by step j-VS+1
-        const int fr = j - C::VS + 1;
-        if (j >= C::VS && !mbar_wait_bounded(bar_step + fr % C::R, (fr / C::R) & 1, abort_flag,
-                                             &g_wait_limit_ns))
-          break;
-        mbar_arrive_expect_tx(bar_v_full + st, C::KV_BYTES);
-        if constexpr (PAGED) {
-          int tok[kBN / 16];
-#pragma unroll
-          for (int i = 0; i < kBN / 16; ++i) tok[i] = paged_box_coord(p, table, j * kBN + i * 16, N);
-#pragma unroll
-          for (int c = 0; c < C::KCH; ++c)
-#pragma unroll
-            for (int i = 0; i < kBN / 16; ++i)
-              tma_load_4d(sV + st * C::KV_BYTES + c * kBN * 128 + i * 16 * 128, &tm_v,
-                          bar_v_full + st, c * 64, kvh, tok[i], 0);
-        } else {
-#pragma unroll
-          for (int c = 0; c < C::KCH; ++c)
-            tma_load_4d(sV + st * C::KV_BYTES + c * kBN * 128, &tm_v, bar_v_full + st, c * 64,
-                        j * kBN, kvh, b);
-        }
-        issued = j + 1;
-      }
-      if (*abort_flag) {
-        for (int j = issued - 1; j >= 0 && j >= issued - C::VS; --j)
-          mbar_wait_timeout(bar_v_full + (j % C::VS), (j / C::VS) & 1, kWaitLimitNs);
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer
+   } else {
+    // ------------------------------------------------ MMA issuer (warp 1)
     // The whole warp runs the issue loop (waits, probes, control flow) and one
     // elected lane issues each tcgen05 instruction. Measured on B200 with the
     // loop on a single lane instead, the per-group commits and waits cost ~40%
     // of the tensor core's throughput (91 instead of 64 cycles per MMA).
-    if (n_kv_max > 0) {
-      constexpr int fmt = BF16 ? 1 : 0;
-      constexpr uint32_t idesc_s = umma_idesc_f16(kBM, kBN, fmt, 0, 0);
-      constexpr uint32_t idesc_o = umma_idesc_f16(kBM, D, fmt, 0, 1);
-      // Descriptors are built once; each MMA only adds its byte offset (>> 4) to the
-      // 14-bit start-address field.
-      const uint64_t dq0 = umma_smem_desc(smem_u32(sQ), 16, 1024);
-      const uint64_t dk0 = umma_smem_desc(smem_u32(sK), 16, 1024);
-      const uint64_t dv0 = umma_smem_desc(smem_u32(sV), kBN * 128, 1024);
-      auto commit = [](uint64_t* bar) {
-        if (elect_one_sync()) umma_commit(bar);
-      };
-      auto wait = [&](uint64_t* bar, uint32_t parity) {
-        return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, &g_wait_limit_ns));
-      };
-      auto test = [](uint64_t* bar, uint32_t parity) {
-        return __all_sync(0xffffffffu, mbar_test(bar, parity));
-      };
-      // `probe` runs after the fifth MMA of a group, while the warp waits for the
-      // tensor core to accept the rest
-      auto issue_s = [&](int t, int j, auto&& probe) {
-        const int st = j % C::KS;
-        const uint32_t s_col = t ? C::TM_S1 : C::TM_S0;
-        const uint64_t aq = dq0 + static_cast<uint64_t>((t * C::Q_BYTES) >> 4);
-        const uint64_t bk = dk0 + static_cast<uint64_t>((st * C::KV_BYTES) >> 4);
+    constexpr int fmt = BF16 ? 1 : 0;
+    constexpr uint32_t idesc_s = umma_idesc_f16(kBM, kBN, fmt, 0, 0);
+    constexpr uint32_t idesc_o = umma_idesc_f16(kBM, D, fmt, 0, 1);
+    // Descriptors are built once; each MMA only adds its byte offset (>> 4) to the
+    // 14-bit start-address field.
+    const uint64_t dq0 = umma_smem_desc(smem_u32(sQ), 16, 1024);
+    const uint64_t dk0 = umma_smem_desc(smem_u32(sK), 16, 1024);
+    const uint64_t dv0 = umma_smem_desc(smem_u32(sV), kBN * 128, 1024);
+    auto commit = [](uint64_t* bar) {
+      if (elect_one_sync()) umma_commit(bar);
+    };
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu,
+                        mbar_wait_bounded(bar, parity, abort_flag, &g_wait_limit_ns));
+    };
+    auto test = [](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_test(bar, parity));
+    };
+    // S_t = Q_t K_g^T for the CTA's g-th key tile
+    auto issue_s = [&](int t, int g) {
+      const int st = g % C::KS;
+      const uint32_t s_col = t ? C::TM_S1 : C::TM_S0;
+      const uint64_t aq = dq0 + static_cast<uint64_t>((t * C::Q_BYTES) >> 4);
+      const uint64_t bk = dk0 + static_cast<uint64_t>((st * C::KV_BYTES) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          constexpr int kRow = kBM * 128;
-          const uint32_t off = ((kk >> 2) * kRow + (kk & 3) * 32) >> 4;
-          if (elect_one_sync()) umma_ss(tmem + s_col, aq + off, bk + off, idesc_s, kk > 0 ? 1u : 0u);
-          if (kk == 4) probe();
-        }
-      };
-      // O_t += P_t V_j in two halves of 64 keys, each behind its half of P
-      auto issue_pv = [&](int t, int j, auto&& probe) {
-        const int st = j % C::VS;
-        const uint32_t p_col = tmem + (t ? C::TM_S1 : C::TM_S0);
-        const uint32_t o_col = tmem + (t ? C::TM_O1 : C::TM_O0);
-        const uint64_t bv = dv0 + static_cast<uint64_t>((st * C::KV_BYTES) >> 4);
-        const uint32_t acc0 = j > 0 ? 1u : 0u;
-        if (!wait(bar_pa_full + t, j & 1)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kBN / 32; ++kk) {
-          if (elect_one_sync())
-            umma_ts(o_col, p_col + kk * 8, bv + ((kk * 16 * 128) >> 4), idesc_o,
-                    kk > 0 ? 1u : acc0);
-          if (kk == 2) probe();
-        }
-        if (!wait(bar_p_full + t, j & 1)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = kBN / 32; kk < kBN / 16; ++kk) {
-          if (elect_one_sync())
-            umma_ts(o_col, p_col + kk * 8, bv + ((kk * 16 * 128) >> 4), idesc_o, 1u);
-        }
-        if (j == n_kv[t] - 1) commit(bar_o_final + t);
-        return true;
-      };
-      auto no_probe = [] {};
-
-      bool ok = wait(bar_q_ready, 0) && wait(bar_k_full, 0);
-      if (ok) {
-        tc_fence_after();
-        if (n_kv[0] > 0) {
-          issue_s(0, 0, no_probe);
-          commit(bar_s0_full);
-        }
-        if (n_kv[1] > 0) issue_s(1, 0, no_probe);
-        commit(bar_step);
+      for (int kk = 0; kk < D / 16; ++kk) {
+        constexpr int kRow = kBM * 128;
+        const uint32_t off = ((kk >> 2) * kRow + (kk & 3) * 32) >> 4;
+        if (elect_one_sync()) umma_ss(tmem + s_col, aq + off, bk + off, idesc_s, kk > 0 ? 1u : 0u);
       }
-      bool v_seen = false;  // V_j's barrier already observed complete
-      for (int j = 0; ok && j < n_kv_max; ++j) {
-        const int jn = j + 1;
-        const int stn = jn % C::KS;  // K stage of tile j + 1
-        const uint32_t phn = (jn / C::KS) & 1;
+    };
+    // O_t += P_t V_g in two halves of 64 keys, each behind its half of P; `pc`
+    // counts the P tiles tile t published before this one, `last` marks the
+    // unit's last PV of the tile. `probe` runs while the tensor core takes the
+    // first half.
+    auto issue_pv = [&](int t, int j, int g, int pc, bool last, auto&& probe) {
+      const int st = g % C::VS;
+      const uint32_t p_col = tmem + (t ? C::TM_S1 : C::TM_S0);
+      const uint32_t o_col = tmem + (t ? C::TM_O1 : C::TM_O0);
+      const uint64_t bv = dv0 + static_cast<uint64_t>((st * C::KV_BYTES) >> 4);
+      const uint32_t acc0 = j > 0 ? 1u : 0u;
+      if (!wait(bar_pa_full + t, pc & 1)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < kBN / 32; ++kk) {
+        if (elect_one_sync())
+          umma_ts(o_col, p_col + kk * 8, bv + ((kk * 16 * 128) >> 4), idesc_o,
+                  kk > 0 ? 1u : acc0);
+        if (kk == 2) probe();
+      }
+      if (!wait(bar_p_full + t, pc & 1)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int kk = kBN / 32; kk < kBN / 16; ++kk) {
+        if (elect_one_sync())
+          umma_ts(o_col, p_col + kk * 8, bv + ((kk * 16 * 128) >> 4), idesc_o, 1u);
+      }
+      if (last) commit(bar_o_final + t);
+      return true;
+    };
+    int kt = 0, qi = 0, pc0 = 0, pc1 = 0;
+    bool ok = true;
+    for (int r = 0; ok; ++r) {
+      const int u = pf_unit_index(r, n_units);
+      if (u == -2) break;
+      if (u < 0) continue;
+      const PfUnit w = pf_unit<PAGED>(p, u);
+      if (w.n == 0) continue;
+      const int n = w.n;
+      ok = wait(bar_q_ready, qi & 1) && wait(bar_k_full + kt % C::KS, (kt / C::KS) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      if (w.n_kv[0] > 0) {
+        issue_s(0, kt);
+        commit(bar_s0_full);
+      }
+      if (w.n_kv[1] > 0) issue_s(1, kt);
+      commit(bar_step + kt % C::R);
+      if (n == 1) commit(bar_q_free);
+      bool v_seen = false;  // V_g's barrier already observed complete
+      for (int j = 0; j < n; ++j) {
+        const int g = kt + j, gn = g + 1, jn = j + 1;
+        const int stn = gn % C::KS;  // K stage of the next key tile
+        const uint32_t phn = (gn / C::KS) & 1;
         bool k_seen = false;
-        if (!v_seen && !(ok = wait(bar_v_full + j % C::VS, (j / C::VS) & 1))) break;
-        if (j < n_kv[0] && !(ok = issue_pv(0, j, [&] {
-              if (jn < n_kv_max) k_seen = test(bar_k_full + stn, phn);
-            })))
+        if (!v_seen && !(ok = wait(bar_v_full + g % C::VS, (g / C::VS) & 1))) break;
+        if (j < w.n_kv[0] &&
+            !(ok = issue_pv(0, j, g, pc0 + j, j == w.n_kv[0] - 1, [&] {
+                if (jn < n) k_seen = test(bar_k_full + stn, phn);
+              })))
           break;
-        if (jn < n_kv_max) {
+        if (jn < n) {
           if (!k_seen && !(ok = wait(bar_k_full + stn, phn))) break;
-          if (jn < n_kv[0]) {
-            issue_s(0, jn, no_probe);
+          if (jn < w.n_kv[0]) {
+            issue_s(0, gn);
             commit(bar_s0_full);
           }
         }
         v_seen = false;
         auto probe_v = [&] {
-          if (jn < n_kv_max) v_seen = test(bar_v_full + jn % C::VS, (jn / C::VS) & 1);
+          if (jn < n) v_seen = test(bar_v_full + gn % C::VS, (gn / C::VS) & 1);
         };
-        if (j < n_kv[1] && !(ok = issue_pv(1, j, probe_v))) break;
-        if (jn < n_kv_max) {
-          if (jn < n_kv[1]) issue_s(1, jn, no_probe);
-          commit(bar_step + jn % C::R);
+        if (j < w.n_kv[1] && !(ok = issue_pv(1, j, g, pc1 + j, j == w.n_kv[1] - 1, probe_v)))
+          break;
+        if (jn < n) {
+          if (jn < w.n_kv[1]) issue_s(1, gn);
+          commit(bar_step + gn % C::R);
+          if (jn == n - 1) commit(bar_q_free);  // the unit's last S MMAs are issued
         }
       }
-      if (!ok) {
-        if (lane == 0) raise_status(CIE_DEV_TIMEOUT);
-        commit(bar_drain);  // all MMAs issued so far must finish before TMEM is freed
-        mbar_wait_timeout(bar_drain, 0, kWaitLimitNs);
-      }
+      kt += n;
+      ++qi;
+      pc0 += w.n_kv[0];
+      pc1 += w.n_kv[1];
+    }
+    if (!ok) {
+      if (lane == 0) raise_status(CIE_DEV_TIMEOUT);
+      commit(bar_drain);  // all MMAs issued so far must finish before TMEM is freed
+      mbar_wait_timeout(bar_drain, 0, kWaitLimitNs);
     }
    }
   } else {
@@ -470,47 +635,50 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int wq = warp & 3;             // TMEM lane quarter this warp may access
     const int row = wq * 32 + lane;      // query row within the tile == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
-    const int gm = m0 + t * kBM + row;   // global query index
-    const int nkv = n_kv[t];
     const uint32_t s_col = t ? C::TM_S1 : C::TM_S0;
     const uint32_t o_col = t ? C::TM_O1 : C::TM_O0;
     using elem_t = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    bool ok = true;
-
-    if (n_kv_max > 0) {
-      ok = mbar_wait_bounded(bar_q_full, 0, abort_flag, &g_wait_limit_ns);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok && p.cos != nullptr && gm < p.M) {
-        int pos = (PAGED ? N - p.M : p.rope_q_pos0) + gm;
-        if (pos < 0 || pos >= p.rope_max_pos) {
-          raise_status(CIE_DEV_BAD_POSITION);
-          pos = pos < 0 ? 0 : p.rope_max_pos - 1;
-        }
-        rope_q_row<D, BF16>(sQ + t * C::Q_BYTES, row, pos, p.cos, p.sin);
-        fence_proxy_async_smem();
+    if constexpr (PAGED) {
+      if (threadIdx.x == 128) {
+        for (int b = 0; b < p.B; ++b)
+          if (p.kv_lens[b] > p.max_blocks * p.block_size) raise_status(CIE_DEV_BAD_BLOCK_ID);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_q_ready);
     }
-
-    if (nkv == 0) {
-      // no visible keys: N == 0 -> zeros (matches the fp32 reference), else NaN rows
-      if (gm < p.M) {
-        elem_t* o = reinterpret_cast<elem_t*>(p.o) + b * p.o_sb + h * p.o_sh + gm * p.o_sm;
-        const float fill = (N == 0) ? 0.f : __int_as_float(0x7fc00000);
-        for (int d = 0; d < D; ++d) {
-          if constexpr (BF16) o[d] = __float2bfloat16_rn(fill);
-          else o[d] = __float2half_rn(fill);
+    int kt = 0, sc = 0, of = 0;  // key steps, S tiles of this tile, finished units before
+    bool ok = true;
+    for (int r = 0; ok; ++r) {
+      const int u = pf_unit_index(r, n_units);
+      if (u == -2) break;
+      if (u < 0) continue;
+      const PfUnit w = pf_unit<PAGED>(p, u);
+      const int gm = w.m0 + t * kBM + row;   // global query index
+      const int nkv = w.n_kv[t];
+      if (nkv == 0) {
+        // no visible keys: N == 0 -> zeros (matches the fp32 reference), else NaN rows
+        if (gm < p.M) {
+          elem_t* o = reinterpret_cast<elem_t*>(p.o) + w.b * p.o_sb + w.h * p.o_sh + gm * p.o_sm;
+          const float fill = (w.N == 0) ? 0.f : __int_as_float(0x7fc00000);
+          for (int d = 0; d < D; ++d) {
+            if constexpr (BF16) o[d] = __float2bfloat16_rn(fill);
+            else o[d] = __float2half_rn(fill);
+          }
         }
+        if (p.n_peers > 0) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_o_stored + t);
+        }
+        kt += w.n;
+        continue;
       }
-    } else if (ok) {
-      const int lim = p.causal ? (N - p.M + gm) : (N - 1);  // keys <= lim are visible
+      const int lim = p.causal ? (w.N - p.M + gm) : (w.N - 1);  // keys <= lim are visible
       float m_run = -INFINITY;  // running max, log2 domain, scaled
       float l_run = 0.f;
       float sv[kBN];
       for (int j = 0; ok && j < nkv; ++j) {
-        ok = t ? mbar_wait_bounded(bar_step + j % C::R, (j / C::R) & 1, abort_flag, &g_wait_limit_ns)
-               : mbar_wait_bounded(bar_s0_full, j & 1, abort_flag, &g_wait_limit_ns);
+        const int g = kt + j;
+        ok = t ? mbar_wait_bounded(bar_step + g % C::R, (g / C::R) & 1, abort_flag,
+                                   &g_wait_limit_ns)
+               : mbar_wait_bounded(bar_s0_full, (sc + j) & 1, abort_flag, &g_wait_limit_ns);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -537,9 +705,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         };
         auto row_max_scaled = [&]() {
 #pragma unroll
-          for (int w = CIE_MAX_CHAINS / 2; w >= 1; w /= 2)
+          for (int wv = CIE_MAX_CHAINS / 2; wv >= 1; wv /= 2)
 #pragma unroll
-            for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+            for (int i = 0; i < wv; ++i) mx[i] = fmaxf(mx[i], mx[i + wv]);
           return mx[0] * p.scale_log2;
         };
         // Lazy rescale: only rows whose max grew by more than 2^8 move their
@@ -634,13 +802,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
 
       if (ok) {
-        ok = mbar_wait_bounded(bar_o_final + t, 0, abort_flag, &g_wait_limit_ns);
+        ok = mbar_wait_bounded(bar_o_final + t, of & 1, abort_flag, &g_wait_limit_ns);
         ok = __all_sync(0xffffffffu, ok);
       }
       if (ok) {
+        // O_t of this unit out of TMEM; the next unit's first PV_t, which
+        // overwrites it, waits for this warpgroup's next P
         tc_fence_after();
         const float inv_l = (l_run > 0.f) ? 1.0f / l_run : __int_as_float(0x7fc00000);
-        elem_t* o = reinterpret_cast<elem_t*>(p.o) + b * p.o_sb + h * p.o_sh + gm * p.o_sm;
+        elem_t* o = reinterpret_cast<elem_t*>(p.o) + w.b * p.o_sb + w.h * p.o_sh + gm * p.o_sm;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t ov[32];
@@ -658,7 +828,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
           }
         }
+        tc_fence_before();
+        if (p.n_peers > 0) {
+          // the rows are in o: hand them to the copy warp
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_o_stored + t);
+        }
       }
+      kt += w.n;
+      sc += nkv;
+      ++of;
     }
     if (!ok) raise_status(CIE_DEV_TIMEOUT);
   }
@@ -702,7 +881,8 @@ static int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CU
   constexpr int smem = PfCfg<D>::SMEM;
   auto kern = prefill_attn_kernel<D, BF16, PAGED>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  const int grid = prm.n_pairs * prm.B * prm.Hq;
+  // persistent: one CTA per SM (225 KB of shared memory each) walks the work list
+  const int grid = prm.n_units < num_sms() ? prm.n_units : num_sms();
   kern<<<grid, kPfThreads, smem, st>>>(mq, mk, mv, prm);
   CIE_CHECK_LAUNCH("prefill_attn_kernel");
   return CIE_OK;
@@ -753,6 +933,7 @@ int paged_prefill_tcgen05(const void* q, const void* k_pool, const void* v_pool,
   prm.N = 0;
   prm.G = Hq / Hkv;
   prm.n_pairs = (M + 2 * kBM - 1) / (2 * kBM);
+  prm.n_units = prm.n_pairs * B * Hq;
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
   prm.o = o;
@@ -806,13 +987,13 @@ extern "C" size_t cie_prefill_attn_workspace(int B, int Hq, int Hkv, int M, int 
   return bytes > 0 ? bytes + 256 : 0;
 }
 
-extern "C" int cie_prefill_attn(const void* q, const void* k, const void* v, void* o, int B,
-                                int Hq, int Hkv, int M, int N, int d, const int64_t* q_strides,
-                                const int64_t* k_strides, const int64_t* v_strides,
-                                const int64_t* o_strides, float scale, int causal, int dtype,
-                                const float* rope_cos, const float* rope_sin, int rope_max_pos,
-                                int rope_q_pos0, int rope_k, void* workspace,
-                                size_t workspace_bytes, void* stream) {
+static int prefill_impl(const void* q, const void* k, const void* v, void* o, int B, int Hq,
+                        int Hkv, int M, int N, int d, const int64_t* q_strides,
+                        const int64_t* k_strides, const int64_t* v_strides,
+                        const int64_t* o_strides, float scale, int causal, int dtype,
+                        const float* rope_cos, const float* rope_sin, int rope_max_pos,
+                        int rope_q_pos0, int rope_k, void* workspace, size_t workspace_bytes,
+                        void* const* o_peers, int n_peers, void* stream) {
   CIE_CHECK_ARG(q && o && (N == 0 || (k && v)), "cie_prefill_attn: null tensor pointer");
   CIE_CHECK_ARG(q_strides && k_strides && v_strides && o_strides,
                 "cie_prefill_attn: null strides");
@@ -876,6 +1057,11 @@ extern "C" int cie_prefill_attn(const void* q, const void* k, const void* v, voi
     ks = q_strides;
     v_strides = q_strides;
   }
+  if (n_peers > 0 && (N == 0 || !use_tcgen05(Hq, Hkv, M, d))) {
+    set_error("cie_prefill_attn_peers: the peer all-gather needs the tcgen05 path (d 64 or 128, "
+              "more than 64 query rows per kv head, N > 0)");
+    return CIE_ERR_UNSUPPORTED;
+  }
   if (N == 0 || !use_tcgen05(Hq, Hkv, M, d))
     return dense_mma_attn(q, kk, v, o, B, Hq, Hkv, M, N, d, q_strides, ks, v_strides, o_strides,
                           scale, causal, bf16, rope_cos, rope_sin, rope_max_pos, q_pos0_eff, ws,
@@ -889,6 +1075,7 @@ extern "C" int cie_prefill_attn(const void* q, const void* k, const void* v, voi
   prm.N = N;
   prm.G = Hq / Hkv;
   prm.n_pairs = (M + 2 * kBM - 1) / (2 * kBM);
+  prm.n_units = prm.n_pairs * B * Hq;
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
   prm.o = o;
@@ -899,6 +1086,8 @@ extern "C" int cie_prefill_attn(const void* q, const void* k, const void* v, voi
   prm.sin = rope_sin;
   prm.rope_max_pos = rope_max_pos;
   prm.rope_q_pos0 = rope_q_pos0;
+  prm.n_peers = n_peers;
+  for (int i = 0; i < n_peers; ++i) prm.o_peers[i] = o_peers[i];
 
   CUtensorMap mq, mk, mv;
   int rc;
@@ -916,4 +1105,35 @@ extern "C" int cie_prefill_attn(const void* q, const void* k, const void* v, voi
                 : launch_prefill<64, false>(mq, mk, mv, prm, st);
   return bf16 ? launch_prefill<128, true>(mq, mk, mv, prm, st)
               : launch_prefill<128, false>(mq, mk, mv, prm, st);
+}
+
+extern "C" int cie_prefill_attn(const void* q, const void* k, const void* v, void* o, int B,
+                                int Hq, int Hkv, int M, int N, int d, const int64_t* q_strides,
+                                const int64_t* k_strides, const int64_t* v_strides,
+                                const int64_t* o_strides, float scale, int causal, int dtype,
+                                const float* rope_cos, const float* rope_sin, int rope_max_pos,
+                                int rope_q_pos0, int rope_k, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  return prefill_impl(q, k, v, o, B, Hq, Hkv, M, N, d, q_strides, k_strides, v_strides,
+                      o_strides, scale, causal, dtype, rope_cos, rope_sin, rope_max_pos,
+                      rope_q_pos0, rope_k, workspace, workspace_bytes, nullptr, 0, stream);
+}
+
+extern "C" int cie_prefill_attn_peers(const void* q, const void* k, const void* v, void* o,
+                                      void* const* o_peers, int n_peers, int B, int Hq, int Hkv,
+                                      int M, int N, int d, const int64_t* q_strides,
+                                      const int64_t* k_strides, const int64_t* v_strides,
+                                      const int64_t* o_strides, float scale, int causal,
+                                      int dtype, const float* rope_cos, const float* rope_sin,
+                                      int rope_max_pos, int rope_q_pos0, int rope_k,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+  CIE_CHECK_ARG(n_peers >= 0 && n_peers <= kMaxPeers,
+                "cie_prefill_attn_peers: n_peers must be in [0, %d]", kMaxPeers);
+  CIE_CHECK_ARG(n_peers == 0 || o_peers != nullptr, "cie_prefill_attn_peers: null o_peers");
+  for (int i = 0; i < n_peers; ++i)
+    CIE_CHECK_ARG(o_peers[i] != nullptr && aligned16(o_peers[i]) && o_peers[i] != o,
+                  "cie_prefill_attn_peers: peer output %d null, unaligned or the local one", i);
+  return prefill_impl(q, k, v, o, B, Hq, Hkv, M, N, d, q_strides, k_strides, v_strides,
+                      o_strides, scale, causal, dtype, rope_cos, rope_sin, rope_max_pos,
+                      rope_q_pos0, rope_k, workspace, workspace_bytes, o_peers, n_peers, stream);
 }

@@ -11,7 +11,10 @@ import ctypes
 import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libcie_attn.so"
+# The in-tree build; CIE_ATTN_LIB names another build of the same library
+# (e.g. one compiled with different tuning macros) to load instead.
+LIB_PATH = Path(os.environ.get("CIE_ATTN_LIB") or
+                Path(__file__).resolve().parent / "libcie_attn.so")
 
 CIE_OK = 0
 CIE_ERR_INVALID = -1
@@ -37,6 +40,10 @@ _i64p = ctypes.POINTER(ctypes.c_int64)
 SIGNATURES: dict[str, tuple] = {
     "cie_prefill_attn": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i64p, _i64p, _i64p,
                               _i64p, _f, _i, _i, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
+    "cie_prefill_attn_peers": (_i, [_vp, _vp, _vp, _vp, ctypes.POINTER(_vp), _i, _i, _i, _i, _i,
+                                    _i, _i, _i64p, _i64p, _i64p, _i64p, _f, _i, _i, _vp, _vp, _i,
+                                    _i, _i, _vp, _sz, _vp]),
+    "cie_peer_barrier": (_i, [ctypes.POINTER(_vp), _i, _i, ctypes.c_uint32, _vp]),
     "cie_prefill_attn_workspace": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i]),
     "cie_paged_attn": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i64p,
                             _i64p, _f, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _vp]),

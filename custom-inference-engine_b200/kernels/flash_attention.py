@@ -93,6 +93,8 @@ def flash_attention(
     rope: tuple[torch.Tensor, torch.Tensor] | None = None,
     rope_q_pos0: int | None = None,
     rope_k: bool = True,
+    out: torch.Tensor | None = None,
+    out_peers: list[int] | None = None,
 ) -> torch.Tensor:
     """Flash attention on CUDA (tcgen05 tensor cores for d in {64, 128}).
 
@@ -103,6 +105,13 @@ def flash_attention(
     query row i is rotated at position ``rope_q_pos0 + i`` (default N - M + i)
     inside the kernel, and keys are rotated at positions 0..N-1 unless
     ``rope_k=False`` (K already rotated, e.g. read from the cache).
+
+    out: optional (B, H, M, D) tensor (any strides, 16-byte aligned rows) to
+    write into instead of a new one. out_peers: device addresses of the same
+    slice in other GPUs' outputs (peer memory mapped into this process); every
+    output tile is then also copied to each of them inside the kernel
+    (``cie_prefill_attn_peers``) and is complete there once every rank has run
+    :func:`peer_barrier` after this call.
     """
     if not q.is_cuda:
         raise RuntimeError("flash_attention requires CUDA tensors")
@@ -133,7 +142,12 @@ def flash_attention(
     q = _kernel_ready(q)
     k = _kernel_ready(k)
     v = _kernel_ready(v)
-    out = torch.empty((B, H, M, D), dtype=q.dtype, device=q.device)
+    if out is None:
+        if out_peers:
+            raise ValueError("out_peers needs an explicit out (the local slice of the output)")
+        out = torch.empty((B, H, M, D), dtype=q.dtype, device=q.device)
+    elif out.shape != (B, H, M, D) or out.dtype != q.dtype or out.device != q.device:
+        raise ValueError(f"out must be a ({B}, {H}, {M}, {D}) {q.dtype} tensor on {q.device}")
     if B == 0 or M == 0 or H == 0:
         return out
     cos, sin, max_pos = _rope_tables(rope, q.device)
@@ -144,14 +158,30 @@ def flash_attention(
     dt = _DTYPES[q.dtype]
     ws_bytes = lib.cie_prefill_attn_workspace(B, H, Hk, M, N, D, dt, do_rope_k)
     ws = _workspace(ws_bytes, q.device)
-    rc = lib.cie_prefill_attn(
-        _vp(q), _vp(k), _vp(v), _vp(out), B, H, Hk, M, N, D,
-        _lib.strides3(q.stride()[:3]), _lib.strides3(k.stride()[:3]),
-        _lib.strides3(v.stride()[:3]), _lib.strides3(out.stride()[:3]),
-        float(scale), 1 if causal else 0, dt, _vp(cos), _vp(sin), max_pos, q_pos0, do_rope_k,
-        _vp(ws), ws_bytes, _stream(q))
+    strides = (_lib.strides3(q.stride()[:3]), _lib.strides3(k.stride()[:3]),
+               _lib.strides3(v.stride()[:3]), _lib.strides3(out.stride()[:3]))
+    tail = (float(scale), 1 if causal else 0, dt, _vp(cos), _vp(sin), max_pos, q_pos0, do_rope_k,
+            _vp(ws), ws_bytes, _stream(q))
+    if out_peers:
+        peers = (ctypes.c_void_p * len(out_peers))(*[int(x) for x in out_peers])
+        rc = lib.cie_prefill_attn_peers(_vp(q), _vp(k), _vp(v), _vp(out), peers, len(out_peers),
+                                        B, H, Hk, M, N, D, *strides, *tail)
+    else:
+        rc = lib.cie_prefill_attn(_vp(q), _vp(k), _vp(v), _vp(out), B, H, Hk, M, N, D, *strides,
+                                  *tail)
     _lib.check(rc, "flash_attention")
     return out
+
+
+def peer_barrier(flag_ptrs: list[int], rank: int, epoch: int, device: torch.device) -> None:
+    """Stream-ordered barrier over the GPUs whose counter arrays ``flag_ptrs`` (one
+    per rank, uint32[world] each, zero-initialised, mapped into this process) name;
+    ``epoch`` grows by one per call. See ``cie_peer_barrier``."""
+    lib = _require()
+    arr = (ctypes.c_void_p * len(flag_ptrs))(*[int(x) for x in flag_ptrs])
+    rc = lib.cie_peer_barrier(arr, len(flag_ptrs), int(rank), ctypes.c_uint32(epoch & 0xFFFFFFFF),
+                              ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+    _lib.check(rc, "peer_barrier")
 
 
 def paged_attention(

@@ -76,6 +76,45 @@ int cie_prefill_attn(const void* q, const void* k, const void* v, void* o,
                      int rope_max_pos, int rope_q_pos0, int rope_k,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * cie_prefill_attn fused with the all-gather of its output across the GPUs of
+ * a kv-head-group sharded prefill (one process per GPU, NVLink peer memory).
+ * Replaces the launch of kernels/flash_attention.py:136-209 on each shard plus
+ * the collective that reassembles [B, S, Hq * d] (the reference is one GPU;
+ * this is the multi-GPU layer).
+ *
+ * Same arguments as cie_prefill_attn; o is this rank's slice of the full
+ * output (its heads), and o_peers[0 .. n_peers) are the same slice in the other
+ * ranks' full outputs, as mapped into this process (e.g. symmetric memory).
+ * Every output tile is written to o and, while the kernel goes on computing,
+ * copied to each peer with 16-byte peer stores. 1 <= n_peers <= 7. Only the
+ * tcgen05 path (d 64 / 128, more than 64 query rows per kv head, N > 0) takes
+ * peers. The peers' rows are complete once every rank's cie_peer_barrier that
+ * follows this call on its stream has returned.
+ */
+int cie_prefill_attn_peers(const void* q, const void* k, const void* v, void* o,
+                           void* const* o_peers, int n_peers,
+                           int B, int Hq, int Hkv, int M, int N, int d,
+                           const int64_t* q_strides, const int64_t* k_strides,
+                           const int64_t* v_strides, const int64_t* o_strides,
+                           float scale, int causal, int dtype,
+                           const float* rope_cos, const float* rope_sin,
+                           int rope_max_pos, int rope_q_pos0, int rope_k,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Stream-ordered barrier across `world` GPUs (one process each) through
+ * counters in peer memory: flags[r] is rank r's array of `world` uint32
+ * counters (zero-initialised, all ranks' arrays mapped into this process);
+ * `epoch` grows by one per call. Publishes epoch into slot `rank` of every
+ * array, then waits (bounded by cie_set_wait_limit; CIE_DEV_TIMEOUT when a
+ * rank does not arrive) until its own array holds epoch in every slot. Work
+ * queued after it on `stream` sees everything the other ranks wrote before
+ * their call. No counterpart in the reference (single GPU).
+ */
+int cie_peer_barrier(uint32_t* const* flags, int world, int rank, uint32_t epoch,
+                     void* stream);
+
 /* Bytes of workspace cie_prefill_attn needs for these arguments: the
  * rotated copy of K when rope_k is set, plus split-KV partials when the call
  * is served by the short-query kernel (G*M <= 64, or d not 64/128). */

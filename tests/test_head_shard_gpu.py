@@ -1,11 +1,14 @@
 """Multi-GPU: kv-head-group sharding gives the one-GPU result, bit for bit.
 
-Two ranks (one process per GPU, NCCL over NVLink) each hold half of the kv-head
-groups of a causal RoPE prefill and of a paged decode batch (pools split by
-head, identical block tables), run the single-GPU kernels on their slice and
-reassemble the output (all-gather, rank-major -> global head order). Every head
-runs the same kernel on the same inputs as on one GPU, so the reassembled output
-must equal the one-GPU output exactly. Skipped with fewer than two GPUs.
+Two ranks (one process per GPU) each hold half of the kv-head groups of a
+causal RoPE prefill and of a paged decode batch (pools split by head, identical
+block tables), run the single-GPU kernels on their slice and reassemble the
+output, two ways: an NCCL all-gather (rank-major -> global head order), and the
+fused path, where the prefill kernel stores each output tile into every rank's
+full output over NVLink (symmetric memory) and a peer barrier closes the step.
+Every head runs the same kernel on the same inputs as on one GPU, so the
+reassembled output must equal the one-GPU output exactly. Skipped with fewer
+than two GPUs.
 """
 
 from __future__ import annotations
@@ -85,6 +88,21 @@ def _worker(rank, world, port, errq):
         gotd = gather_output(od).permute(1, 0, 2, 3, 4).reshape(3, Hq, M, d)
         wantd = paged_attention(qd, kp, vp, tables, kv_lens, True, rope=rope)
         assert torch.equal(gotd, wantd), "sharded paged attention differs from one GPU"
+
+        # the fused path: output tiles stored into every rank's full output by the
+        # kernel itself (symmetric memory), closed by the peer barrier; three steps
+        # so that both alternating buffers are used and one is reused
+        from engine.head_shard import PeerOutput
+
+        po = PeerOutput((B, Hq, S, d), torch.bfloat16, dev)
+        for step in range(3):
+            full = po.attention(local_heads(q, sh, False), local_heads(k, sh, True),
+                                local_heads(v, sh, True), sh, True, rope=rope)
+            torch.cuda.synchronize()
+            assert torch.equal(full, want), f"fused peer gather differs from one GPU (step {step})"
+        from kernels import _lib
+
+        assert _lib.device_status(clear=True) == 0
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as e:  # report to the parent, which fails the test
