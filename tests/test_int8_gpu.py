@@ -139,3 +139,28 @@ def test_layouts_and_errors(cuda):
         int8_matmul(x3, w, s[None])
     with pytest.raises(AssertionError):
         int8_matmul(torch.randn(4, 64, device=cuda, dtype=torch.bfloat16), w, s)
+
+
+def test_unaligned_contiguous_views(cuda):
+    """x and w as contiguous views that start 2 / 1 bytes past a 16-byte boundary
+    (e.g. slices of a flat buffer): the wrapper copies them to aligned storage
+    instead of handing the C ABI an unaligned pointer."""
+    import torch
+
+    from kernels.int8_matmul import int8_matmul
+
+    M, N, K = 5, 256, 128
+    rng = np.random.default_rng(77)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = rng.integers(-128, 128, size=(N, K)).astype(np.int8)
+    s = (rng.random(N) * 0.01 + 1e-3).astype(np.float32)
+    flat_x = torch.zeros(M * K + 1, dtype=torch.bfloat16, device=cuda)
+    tx = flat_x[1:].view(M, K)
+    tx.copy_(torch.from_numpy(x).to(cuda, torch.bfloat16))
+    flat_w = torch.zeros(N * K + 1, dtype=torch.int8, device=cuda)
+    tw = flat_w[1:].view(N, K)
+    tw.copy_(torch.from_numpy(w).to(cuda))
+    assert tx.is_contiguous() and tx.data_ptr() % 16 and tw.data_ptr() % 16
+    y = int8_matmul(tx, tw, torch.from_numpy(s).to(cuda)).float().cpu().numpy()
+    ref = oracle.int8_matmul(tx.float().cpu().numpy(), w, s)
+    _check(y, ref, "bf16", "unaligned views")

@@ -153,6 +153,23 @@ def test_strided_views_like_the_engine(cuda):
     assert_close_attn(to_np(out), ref, what="strided")
 
 
+def test_unaligned_contiguous_view(cuda):
+    """A contiguous q that starts 2 bytes past a 16-byte boundary (a slice of a flat
+    buffer) is copied to aligned storage by the wrapper, not refused by the C ABI."""
+    import torch
+    from kernels.flash_attention import flash_attention
+
+    B, H, Hk, L, D = 1, 8, 2, 300, 64
+    q, k, v = normal(15, (B, H, L, D)), normal(16, (B, Hk, L, D)), normal(17, (B, Hk, L, D))
+    flat = torch.zeros(q.size + 1, dtype=torch.bfloat16, device=cuda)
+    tq = flat[1:].view(B, H, L, D)
+    tq.copy_(to_torch(q, torch.bfloat16, cuda))
+    assert tq.is_contiguous() and tq.data_ptr() % 16
+    out = flash_attention(tq, to_torch(k, torch.bfloat16, cuda), to_torch(v, torch.bfloat16, cuda),
+                          True)
+    assert_close_attn(to_np(out), oracle.attention(q, k, v, causal=True), what="unaligned q")
+
+
 def test_edge_cases(cuda):
     import torch
     from kernels.flash_attention import flash_attention
