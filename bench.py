@@ -75,6 +75,7 @@ METRIC = BASELINE["metric"]
 THETA = 500000.0
 
 HEADLINE = dict(name="cfg4_prefill_llama3_8b", B=4, Hq=32, Hkv=8, S=8192, d=128)
+HEADLINE_FLOPS = 4.0 * 4 * 32 * 128 * 8192 * 8193 / 2
 CFG2 = dict(name="cfg2_prefill_llama32_1b", B=8, Hq=32, Hkv=8, S=2048, d=64)
 CFG3 = dict(name="cfg3_paged_decode", B=64, Hq=32, Hkv=8, M=1, d=64, lo=256, hi=8192, bs=16)
 CFG5 = dict(name="cfg5_spec_verify", B=32, Hq=32, Hkv=8, M=5, d=128, lo=1024, hi=32768, bs=16)
@@ -582,6 +583,33 @@ def e2e_prefill(cfg, world, rank, steps, warmup):
     return prefill_flops(B, cfg["Hq"], S, d) / (ms * 1e-3) / 1e12, h2d, d2h
 
 
+def measure_pcie(world, mib=256, reps=5):
+    """Pinned host<->device copy bandwidth of this rank while every rank copies at
+    the same time (the condition the e2e leg runs in): GB/s H2D and D2H, max time
+    over ranks. It bounds e2e: a step moves h2d + d2h bytes over these links."""
+    import torch
+
+    n = mib * 1024 * 1024
+    host = torch.empty(n, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(n, dtype=torch.uint8, device="cuda")
+    out = {}
+    for name, fn in (("h2d", lambda: dev.copy_(host, non_blocking=True)),
+                     ("d2h", lambda: host.copy_(dev, non_blocking=True))):
+        fn()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(s.elapsed_time(e) / reps, world)
+        out[f"{name}_gbs_per_rank"] = n / (ms * 1e-3) / 1e9
+        out[f"{name}_gbs_all_ranks"] = world * n / (ms * 1e-3) / 1e9
+    del host, dev
+    return out
+
+
 # ---------------------------------------------------------------- CPU baseline
 def _host_cores() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
@@ -972,8 +1000,13 @@ def main():
     if not args.no_e2e:
         n = max(5, min(args.steps, 20))
         ev, h2d, d2h = e2e_prefill(HEADLINE, world, rank, n, 2)
+        pcie = measure_pcie(world)
+        # the copies alone, at the bandwidth every rank gets while all copy at once,
+        # bound the e2e step from below (H2D and D2H overlap each other and the math)
+        t_copy = max(h2d / (pcie["h2d_gbs_all_ranks"] * 1e9), d2h / (pcie["d2h_gbs_all_ranks"] * 1e9))
         e2e = {"value": ev, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "steps": n}
+               "d2h_bytes_per_step": d2h, "steps": n, "pcie": pcie,
+               "copy_bound_value": HEADLINE_FLOPS / t_copy / 1e12}
 
     status = _lib.device_status(clear=True)
     cpu = None

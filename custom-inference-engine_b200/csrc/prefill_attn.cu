@@ -94,7 +94,7 @@ struct PfCfg {
   static constexpr int R = 8;
   static_assert(R > KS && R > VS, "step ring must be deeper than the K/V rings");
   static constexpr int BAR_OFF = 2 * Q_BYTES + (KS + VS) * KV_BYTES;
-  static constexpr int NBARS = 3 + KS + VS + 1 + R + 2 + 2 + 2 + 2 + 1;
+  static constexpr int NBARS = 6 + KS + VS + 1 + R + 2 + 2 + 2 + 2 + 1;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 /*tmem slot, abort*/ + 1024 /*align*/;
   static constexpr uint32_t TM_S0 = 0, TM_S1 = 128;    // P_t aliases cols [0, 64) of S_t
   static constexpr uint32_t TM_O0 = 256, TM_O1 = 256 + D;
@@ -247,10 +247,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint8_t* sK = sQ + 2 * C::Q_BYTES;       // [KS][KCH][128][128B]
   uint8_t* sV = sK + C::KS * C::KV_BYTES;  // [VS][KCH][128][128B]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-  uint64_t* bar_q_full = bars + 0;   // Q tiles of the unit landed
-  uint64_t* bar_q_ready = bars + 1;  // ... and rotated (three loader warps arrive)
-  uint64_t* bar_q_free = bars + 2;   // every S MMA of the unit complete: Q may be replaced
-  uint64_t* bar_k_full = bars + 3;
+  // Per query tile t, counted over the units in which tile t has keys:
+  uint64_t* bar_q_full = bars + 0;   // [2] Q_t of the unit landed
+  uint64_t* bar_q_ready = bars + 2;  // [2] ... and rotated by softmax warpgroup t
+  uint64_t* bar_q_free = bars + 4;   // [2] every S_t MMA of the unit complete: Q_t may go
+  uint64_t* bar_k_full = bars + 6;
   uint64_t* bar_v_full = bar_k_full + C::KS;
   uint64_t* bar_s0_full = bar_v_full + C::VS;  // S0 of a key step complete (and PV0 before it)
   // bar_step[g % R], phase g / R, for the CTA's g-th key step (counted over all
@@ -271,9 +272,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int n_units = p.n_units;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_q_full, 1);
-    mbar_init(bar_q_ready, 2);
-    mbar_init(bar_q_free, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar_q_full + t, 1);
+      mbar_init(bar_q_ready + t, 4);  // one arrive per softmax warp
+      mbar_init(bar_q_free + t, 1);
+    }
     for (int s = 0; s < C::KS; ++s) mbar_init(bar_k_full + s, 1);
     for (int s = 0; s < C::VS; ++s) mbar_init(bar_v_full + s, 1);
     mbar_init(bar_s0_full, 1);
@@ -354,11 +357,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
    } else if (warp != 1) {
     // -------------------------------------- loaders (warp 0: Q and K, warp 2: V)
-    // and RoPE of Q (warps 0 and 2 together). Lane 0 of each issues the TMA
-    // copies; at a unit boundary it first issues the copies whose stages earlier
-    // units free, then the two warps rotate the new Q tiles in shared memory,
-    // then it issues the rest (their stages are freed by this unit's MMAs, which
-    // wait for the rotated Q).
+    // Lane 0 issues the TMA copies. Q_t of a unit is loaded once the previous
+    // unit's last S_t MMA has completed (tile 0 finishes a key step before tile 1
+    // under the causal mask, so its next Q comes in early); stage and step
+    // counters run on across units.
     const bool kload = warp == 0, vload = warp == 2;
     if (lane == 0) {
       if (kload) {
@@ -368,7 +370,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tma_prefetch_desc(&tm_v);
       }
     }
-    int k_issued = 0, v_issued = 0, q_issued = 0;  // totals, for the drain on abort
+    int k_issued = 0, v_issued = 0;  // totals, for the drain on abort
+    int q_issued[2] = {0, 0};
     // K tile g (the CTA's g-th key step) into its stage; j = tile within the unit
     auto load_k = [&](int g, const PfUnit& w, int j) -> bool {
       const int st = g % C::KS;
@@ -424,76 +427,46 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       v_issued = g + 1;
       return true;
     };
-    const int rope_lane = (warp == 0 ? 0 : 32) + lane;
-    int kt = 0, qi = 0;  // key steps and units (with keys) before the current unit
+    int kt = 0;           // key steps before the current unit
+    int qc[2] = {0, 0};   // units before the current one in which tile t had keys
     bool ok = true;
-    for (int r = 0; ok; ++r) {
-      const int u = pf_unit_index(r, n_units);
-      if (u == -2) break;
-      if (u < 0) continue;
-      const PfUnit w = pf_unit<PAGED>(p, u);
-      if (w.n == 0) continue;
-      int kj = 0, vj = 0;  // next K / V tile of the unit
-      if (lane == 0) {
+    if (lane == 0 && (kload || vload)) {
+      for (int r = 0; ok; ++r) {
+        const int u = pf_unit_index(r, n_units);
+        if (u == -2) break;
+        if (u < 0) continue;
+        const PfUnit w = pf_unit<PAGED>(p, u);
+        if (w.n == 0) continue;
         if (kload) {
-          // Q may be replaced once every S MMA of the previous unit completed
-          if (qi > 0)
-            ok = mbar_wait_bounded(bar_q_free, (qi - 1) & 1, abort_flag, &g_wait_limit_ns);
-          if (ok) {
-            mbar_arrive_expect_tx(bar_q_full, 2 * C::Q_BYTES);
 #pragma unroll
-            for (int t = 0; t < 2; ++t)
+          for (int t = 0; t < 2; ++t) {
+            if (w.n_kv[t] == 0) continue;
+            if (qc[t] > 0 &&
+                !(ok = mbar_wait_bounded(bar_q_free + t, (qc[t] - 1) & 1, abort_flag,
+                                         &g_wait_limit_ns)))
+              break;
+            mbar_arrive_expect_tx(bar_q_full + t, C::Q_BYTES);
 #pragma unroll
-              for (int c = 0; c < C::KCH; ++c)
-                tma_load_4d(sQ + t * C::Q_BYTES + c * kBM * 128, &tm_q, bar_q_full, c * 64,
-                            w.m0 + t * kBM, w.h, w.b);
-            q_issued = qi + 1;
+            for (int c = 0; c < C::KCH; ++c)
+              tma_load_4d(sQ + t * C::Q_BYTES + c * kBM * 128, &tm_q, bar_q_full + t, c * 64,
+                          w.m0 + t * kBM, w.h, w.b);
+            q_issued[t] = qc[t] + 1;
           }
-          // K stages freed by earlier units: tiles j < KS
-          for (; ok && kj < w.n && kj < C::KS; ++kj) ok = load_k(kt + kj, w, kj);
-        } else if (vload) {
-          for (; ok && vj < w.n && vj < C::VS - 1; ++vj) ok = load_v(kt + vj, w, vj);
+          for (int j = 0; ok && j < w.n; ++j) ok = load_k(kt + j, w, j);
+        } else {
+          for (int j = 0; ok && j < w.n; ++j) ok = load_v(kt + j, w, j);
         }
+        kt += w.n;
+        qc[0] += w.n_kv[0] > 0;
+        qc[1] += w.n_kv[1] > 0;
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (ok) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait_bounded(bar_q_full, qi & 1, abort_flag, &g_wait_limit_ns));
-      }
-      if (!ok) break;
-      if (p.cos != nullptr) {
-        const int pos0 = PAGED ? w.N - p.M : p.rope_q_pos0;
-        for (int rr = rope_lane; rr < 2 * kBM; rr += 64) {
-          const int t = rr / kBM, row = rr % kBM;
-          const int gm = w.m0 + t * kBM + row;
-          if (gm >= p.M) continue;
-          int pos = pos0 + gm;
-          if (pos < 0 || pos >= p.rope_max_pos) {
-            raise_status(CIE_DEV_BAD_POSITION);
-            pos = pos < 0 ? 0 : p.rope_max_pos - 1;
-          }
-          rope_q_row<D, BF16>(sQ + t * C::Q_BYTES, row, pos, p.cos, p.sin);
-        }
-        fence_proxy_async_smem();
-      }
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar_q_ready);
-        if (kload) {
-          for (; ok && kj < w.n; ++kj) ok = load_k(kt + kj, w, kj);
-        } else if (vload) {
-          for (; ok && vj < w.n; ++vj) ok = load_v(kt + vj, w, vj);
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      kt += w.n;
-      ++qi;
     }
     if (*abort_flag && lane == 0) {
       // let this CTA's copies still in flight land before its smem is released:
       // the newest load of each stage is the latest phase of that stage's barrier
       if (kload) {
-        if (q_issued > 0) mbar_wait_timeout(bar_q_full, (q_issued - 1) & 1, kWaitLimitNs);
+        for (int t = 0; t < 2; ++t)
+          if (q_issued[t] > 0) mbar_wait_timeout(bar_q_full + t, (q_issued[t] - 1) & 1, kWaitLimitNs);
         for (int g = k_issued - 1; g >= 0 && g >= k_issued - C::KS; --g)
           mbar_wait_timeout(bar_k_full + (g % C::KS), (g / C::KS) & 1, kWaitLimitNs);
       } else if (vload) {
@@ -567,7 +540,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (last) commit(bar_o_final + t);
       return true;
     };
-    int kt = 0, qi = 0, pc0 = 0, pc1 = 0;
+    int kt = 0, pc0 = 0, pc1 = 0, qr0 = 0, qr1 = 0;
     bool ok = true;
     for (int r = 0; ok; ++r) {
       const int u = pf_unit_index(r, n_units);
@@ -576,16 +549,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const PfUnit w = pf_unit<PAGED>(p, u);
       if (w.n == 0) continue;
       const int n = w.n;
-      ok = wait(bar_q_ready, qi & 1) && wait(bar_k_full + kt % C::KS, (kt / C::KS) & 1);
+      // qr_t: earlier units in which tile t had keys (one Q_t each)
+      ok = wait(bar_k_full + kt % C::KS, (kt / C::KS) & 1);
       if (!ok) break;
-      tc_fence_after();
       if (w.n_kv[0] > 0) {
+        if (!(ok = wait(bar_q_ready + 0, qr0 & 1))) break;
+        tc_fence_after();
         issue_s(0, kt);
         commit(bar_s0_full);
+        if (w.n_kv[0] == 1) commit(bar_q_free + 0);
       }
-      if (w.n_kv[1] > 0) issue_s(1, kt);
+      if (w.n_kv[1] > 0) {
+        if (!(ok = wait(bar_q_ready + 1, qr1 & 1))) break;
+        tc_fence_after();
+        issue_s(1, kt);
+        if (w.n_kv[1] == 1) commit(bar_q_free + 1);
+      }
       commit(bar_step + kt % C::R);
-      if (n == 1) commit(bar_q_free);
       bool v_seen = false;  // V_g's barrier already observed complete
       for (int j = 0; j < n; ++j) {
         const int g = kt + j, gn = g + 1, jn = j + 1;
@@ -603,6 +583,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           if (jn < w.n_kv[0]) {
             issue_s(0, gn);
             commit(bar_s0_full);
+            if (jn == w.n_kv[0] - 1) commit(bar_q_free + 0);  // tile 0's last S
           }
         }
         v_seen = false;
@@ -612,15 +593,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (j < w.n_kv[1] && !(ok = issue_pv(1, j, g, pc1 + j, j == w.n_kv[1] - 1, probe_v)))
           break;
         if (jn < n) {
-          if (jn < w.n_kv[1]) issue_s(1, gn);
+          if (jn < w.n_kv[1]) {
+            issue_s(1, gn);
+            if (jn == w.n_kv[1] - 1) commit(bar_q_free + 1);  // tile 1's last S
+          }
           commit(bar_step + gn % C::R);
-          if (jn == n - 1) commit(bar_q_free);  // the unit's last S MMAs are issued
         }
       }
       kt += n;
-      ++qi;
       pc0 += w.n_kv[0];
       pc1 += w.n_kv[1];
+      qr0 += w.n_kv[0] > 0;
+      qr1 += w.n_kv[1] > 0;
     }
     if (!ok) {
       if (lane == 0) raise_status(CIE_DEV_TIMEOUT);
@@ -644,7 +628,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           if (p.kv_lens[b] > p.max_blocks * p.block_size) raise_status(CIE_DEV_BAD_BLOCK_ID);
       }
     }
-    int kt = 0, sc = 0, of = 0;  // key steps, S tiles of this tile, finished units before
+    int kt = 0, sc = 0, of = 0;  // key steps, S tiles of this tile, units with keys before
     bool ok = true;
     for (int r = 0; ok; ++r) {
       const int u = pf_unit_index(r, n_units);
@@ -670,6 +654,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         kt += w.n;
         continue;
       }
+      // Q_t of this unit: rotate this thread's row in shared memory, then hand the
+      // tile to the MMA warp
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_q_full + t, of & 1, abort_flag,
+                                                     &g_wait_limit_ns));
+      if (!ok) break;
+      if (p.cos != nullptr && gm < p.M) {
+        int pos = (PAGED ? w.N - p.M : p.rope_q_pos0) + gm;
+        if (pos < 0 || pos >= p.rope_max_pos) {
+          raise_status(CIE_DEV_BAD_POSITION);
+          pos = pos < 0 ? 0 : p.rope_max_pos - 1;
+        }
+        rope_q_row<D, BF16>(sQ + t * C::Q_BYTES, row, pos, p.cos, p.sin);
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_q_ready + t);
       const int lim = p.causal ? (w.N - p.M + gm) : (w.N - 1);  // keys <= lim are visible
       float m_run = -INFINITY;  // running max, log2 domain, scaled
       float l_run = 0.f;
@@ -882,7 +882,12 @@ static int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CU
   auto kern = prefill_attn_kernel<D, BF16, PAGED>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   // persistent: one CTA per SM (225 KB of shared memory each) walks the work list
+  // (CIE_PF_ONE_UNIT_PER_CTA builds the one-unit-per-CTA grid instead, for comparison)
+#ifdef CIE_PF_ONE_UNIT_PER_CTA
+  const int grid = prm.n_units;
+#else
   const int grid = prm.n_units < num_sms() ? prm.n_units : num_sms();
+#endif
   kern<<<grid, kPfThreads, smem, st>>>(mq, mk, mv, prm);
   CIE_CHECK_LAUNCH("prefill_attn_kernel");
   return CIE_OK;
