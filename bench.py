@@ -353,7 +353,7 @@ class PagedWorkload:
     would; the events time the GPU work. The output gather (N > 1) stays eager.
     """
 
-    def __init__(self, cfg, world, rank, seed=0):
+    def __init__(self, cfg, world, rank, seed=0, split_tokens=0, slice_of=0):
         import numpy as np
         import torch
 
@@ -362,7 +362,8 @@ class PagedWorkload:
 
         self.cfg, self.world, self.rank = cfg, world, rank
         B, M, d, bs = cfg["B"], cfg["M"], cfg["d"], cfg["bs"]
-        self.shard = shard_heads(cfg["Hq"], cfg["Hkv"], world, rank)
+        # slice_of > 1 (one GPU, no collectives): rank 0's head slice of a slice_of-way job
+        self.shard = shard_heads(cfg["Hq"], cfg["Hkv"], slice_of or world, rank)
         rng = np.random.default_rng(seed)
         ctx = rng.integers(cfg["lo"], cfg["hi"] + 1, size=B)
         lens = ctx + M
@@ -383,8 +384,9 @@ class PagedWorkload:
         self.kv_lens = torch.from_numpy(lens.astype(np.int32)).cuda()
         self.cos, self.sin = build_rope_cache(int(lens.max()) + 1, d, theta=THETA, device="cuda")
         self.lens = lens
-        H_all = cfg["Hkv"]
-        self.bytes_total = (float(lens.sum()) * H_all * d * 2 * 2 + 2 * B * cfg["Hq"] * M * d * 2 +
+        H_all = cfg["Hkv"] // (slice_of or 1)
+        self.bytes_total = (float(lens.sum()) * H_all * d * 2 * 2 +
+                            2 * B * cfg["Hq"] // (slice_of or 1) * M * d * 2 +
                             tables.size * 4 * world + B * 4 * world)
         self.flops_total = float(sum(4.0 * cfg["Hq"] * d * sum(L - M + i + 1 for i in range(M))
                                      for L in lens))
@@ -397,7 +399,7 @@ class PagedWorkload:
 
         def call():
             return paged_attention(self.q, self.k_pool, self.v_pool, self.tables, self.kv_lens,
-                                   True, rope=(self.cos, self.sin))
+                                   True, rope=(self.cos, self.sin), split_tokens=split_tokens)
 
         call()  # first call outside the capture (kernel attributes, tensor maps)
         torch.cuda.synchronize()
@@ -857,7 +859,7 @@ def run_only(args, world, rank):
         wl = PrefillWorkload(cfg, world, rank)
         unit, work = "TFLOP/s", wl.flops_total / 1e12
     else:
-        wl = PagedWorkload(cfg, world, rank)
+        wl = PagedWorkload(cfg, world, rank, split_tokens=args.split, slice_of=args.slice_of)
         unit, work = "GB/s", wl.bytes_total / 1e9
     total, kms = time_steps(wl, args.steps, args.warmup, world)
     if rank == 0:
@@ -887,6 +889,11 @@ def main():
                          "(default) or NCCL all_gather_into_tensor")
     ap.add_argument("--batch", type=int, default=0,
                     help="with --only: override the batch size (smaller ncu captures)")
+    ap.add_argument("--split", type=int, default=0,
+                    help="with --only cfg3/cfg5: split-KV partition size (0: automatic)")
+    ap.add_argument("--slice-of", type=int, default=0,
+                    help="with --only cfg3/cfg5 on one GPU: time rank 0's head slice of an "
+                         "N-way job")
     ap.add_argument("--cpu-worker", default="", help=argparse.SUPPRESS)
     ap.add_argument("--cpu-seconds", type=float, default=1.0, help=argparse.SUPPRESS)
     args = ap.parse_args()
