@@ -689,14 +689,16 @@ static int pick_mt(int R, int d) {
 
 static int auto_split_tokens(int64_t units, int max_len, int d) {
   // Lengths are only known on the device, so partitions are sized from the
-  // table width: about 14 partitions per SM over the batch if every sequence
-  // were full (measured on B200: decode and verify both peak there), never
-  // below 256 / 1024 tokens (so the partial-result traffic stays around 1% of
-  // the K/V bytes), at most 4096.
+  // table width: about 7 partitions per SM over the batch if every sequence
+  // were full (14 once there are more than two (sequence, kv head, row group)
+  // units per SM), never below 512 tokens at d <= 64 / 2048 at d >= 128, at
+  // most 4096. Measured on B200 (decode d=64 and verify d=128, full batch and
+  // one rank's head slice at 2, 4 and 8 GPUs): shorter partitions lose more to
+  // each CTA's pipeline start and to the merge than they gain in parallelism.
   const int sms = num_sms();
-  const int per_sm = 14;
+  const int per_sm = units > 2 * sms ? 14 : 7;
   int64_t want = (static_cast<int64_t>(max_len) * units) / (static_cast<int64_t>(sms) * per_sm);
-  const int lo = (d >= 128) ? 1024 : 256;
+  const int lo = (d >= 128) ? 2048 : 512;
   if (want < lo) want = lo;
   if (want > 4096) want = 4096;
   want = ((want + 63) / 64) * 64;

@@ -240,11 +240,11 @@ def test_config5_full_size_sampled(cuda, hkv, split):
     """speculative verify, B=32, M=5, ctx ~ U[1024, 32768], d=128, block
     size 16, random-permutation tables, at full size; checked on sampled sequences
     (shortest, longest and three more) against the oracle. ``one_kv_head_slice`` is
-    what one rank of eight holds (Hq=4, Hkv=1): the automatic plan then makes more
-    partitions than the merge kernel's shared-memory path takes, so the partitions
-    are merged by its fallback path on full-length data (sequence 0 is given the
-    longest context the config allows, 32768, so that it has 33 partitions; with
-    512-token partitions every sequence has more than 32)."""
+    what one rank of eight holds (Hq=4, Hkv=1), with the automatic partition size;
+    with 512-token partitions every sequence (sequence 0 is given the longest
+    context the config allows, 32768: 65 partitions) has more partitions than the
+    merge kernel's shared-memory path takes (32), so they are merged by its
+    fallback path on full-length data."""
     import torch
     from kernels import _lib, build_rope_cache
     from kernels.flash_attention import paged_attention
