@@ -94,8 +94,8 @@ struct PfCfg {
   static constexpr int R = 8;
   static_assert(R > KS && R > VS, "step ring must be deeper than the K/V rings");
   static constexpr int BAR_OFF = 2 * Q_BYTES + (KS + VS) * KV_BYTES;
-  static constexpr int NBARS = 6 + KS + VS + 1 + R + 2 + 2 + 2 + 2 + 1;
-  static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 /*tmem slot, abort*/ + 1024 /*align*/;
+  static constexpr int NBARS = 6 + KS + VS + 1 + R + 2 + 2 + 2 + 1;
+  static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 /*tmem slot, abort flag, stored counters*/ + 1024 /*align*/;
   static constexpr uint32_t TM_S0 = 0, TM_S1 = 128;    // P_t aliases cols [0, 64) of S_t
   static constexpr uint32_t TM_O0 = 256, TM_O1 = 256 + D;
   static constexpr uint32_t TM_COLS = 512;
@@ -262,10 +262,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* bar_pa_full = bar_step + C::R;  // [2] per tile: P keys 0..63 written
   uint64_t* bar_p_full = bar_pa_full + 2;   // [2] per tile: all of P written
   uint64_t* bar_o_final = bar_p_full + 2;   // [2] per tile: last PV of the unit complete
-  uint64_t* bar_o_stored = bar_o_final + 2; // [2] per tile: the unit's rows are in o
-  uint64_t* bar_drain = bar_o_stored + 2;   // [1] abort path only
+  uint64_t* bar_drain = bar_o_final + 2;    // [1] abort path only
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // [2] per tile: warps of the softmax warpgroup that stored a unit's rows to o
+  // (4 per unit). A counter, not an mbarrier: the copy warp may fall several
+  // units behind, and a counter cannot alias phases.
+  volatile uint32_t* stored = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -287,10 +290,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(bar_pa_full + t, 4);
       mbar_init(bar_p_full + t, 4);
       mbar_init(bar_o_final + t, 1);
-      mbar_init(bar_o_stored + t, 4);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
+    stored[0] = 0;
+    stored[1] = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -312,28 +316,49 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // unit. Idle when there are no peers.
     if (p.n_peers > 0) {
       bool ok = true;
-      int ui = 0;  // units of this CTA so far (every unit, with keys or not)
+      uint32_t ui = 0;  // units of this CTA so far (every unit, with keys or not)
       using vec_t = uint4;
+      constexpr int kVec = 8;  // 16-byte loads in flight per lane
+      // wait (bounded, sleeping between polls so the softmax warps sharing this
+      // scheduler keep their issue slots) until tile t's rows of unit ui are in o
+      auto wait_stored = [&](int t, uint32_t target) -> bool {
+        if (stored[t] >= target) return true;
+        const uint64_t limit = *reinterpret_cast<const volatile uint64_t*>(&g_wait_limit_ns);
+        if (limit == 0) {
+          *abort_flag = 1;
+          return false;
+        }
+        const uint64_t t0 = globaltimer_ns();
+        while (stored[t] < target) {
+          if (*abort_flag) return false;
+          if (globaltimer_ns() - t0 > limit) {
+            *abort_flag = 1;
+            return false;
+          }
+          __nanosleep(128);
+        }
+        return true;
+      };
       for (int r = 0; ok; ++r) {
         const int u = pf_unit_index(r, n_units);
         if (u == -2) break;
         if (u < 0) continue;
         const PfUnit w = pf_unit<PAGED>(p, u);
         for (int t = 0; t < 2 && ok; ++t) {
-          ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_o_stored + t, ui & 1, abort_flag,
-                                                         &g_wait_limit_ns));
+          ok = __all_sync(0xffffffffu, wait_stored(t, 4 * (ui + 1)));
           if (!ok) break;
+          __threadfence_block();  // the softmax warps' stores of these rows are visible
           const int mt0 = w.m0 + t * kBM;
           const int rows = min(kBM, p.M - mt0);
           if (rows <= 0) continue;
           constexpr int CH = D * 2 / 16;  // 16-byte chunks per row
           const int64_t base = static_cast<int64_t>(w.b) * p.o_sb + w.h * p.o_sh;
           const uint8_t* src = reinterpret_cast<const uint8_t*>(p.o);
-          for (int q0 = lane; q0 < rows * CH; q0 += 32 * 4) {
-            vec_t v[4];
-            int64_t off[4];
+          for (int q0 = lane; q0 < rows * CH; q0 += 32 * kVec) {
+            vec_t v[kVec];
+            int64_t off[kVec];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
+            for (int i = 0; i < kVec; ++i) {
               const int q = q0 + 32 * i;
               off[i] = -1;
               if (q < rows * CH) {
@@ -344,7 +369,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             for (int pe = 0; pe < p.n_peers; ++pe) {
               uint8_t* dst = reinterpret_cast<uint8_t*>(p.o_peers[pe]);
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
+              for (int i = 0; i < kVec; ++i)
                 if (off[i] >= 0) *reinterpret_cast<vec_t*>(dst + off[i]) = v[i];
             }
           }
@@ -648,8 +673,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           }
         }
         if (p.n_peers > 0) {
+          __threadfence_block();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_o_stored + t);
+          if (lane == 0) atomicAdd(const_cast<uint32_t*>(stored + t), 1u);
         }
         kt += w.n;
         continue;
@@ -831,8 +857,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tc_fence_before();
         if (p.n_peers > 0) {
           // the rows are in o: hand them to the copy warp
+          __threadfence_block();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_o_stored + t);
+          if (lane == 0) atomicAdd(const_cast<uint32_t*>(stored + t), 1u);
         }
       }
       kt += w.n;

@@ -240,3 +240,37 @@ def test_full_size_configs_sampled_rows(cuda, cfg):
             errs.append((out[b, h, rows].float() - ref).abs())
     err = torch.cat([e.flatten() for e in errs])
     assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3, (err.max().item(), err.mean().item())
+
+
+@pytest.mark.parametrize("n_copies", [1, 7])
+def test_output_copies_inside_the_kernel(cuda, n_copies):
+    """cie_prefill_attn_peers on one GPU: the 'peer' outputs are other buffers of
+    the same device, so the copy warp's path (its counters, the copy loop, the final
+    fence) runs without a second GPU. Short units (S = 512) and seven copies make
+    the copy warp fall several units behind the softmax warpgroups, the case its
+    counters exist for. Every copy must equal the local output bit for bit, and the
+    local output must match the oracle."""
+    import torch
+    from kernels import _lib, build_rope_cache
+    from kernels.flash_attention import flash_attention
+
+    _lib.device_status(clear=True)
+    # 512 one-pair units over at most 148 CTAs: each CTA walks several of them
+    B, H, Hk, S, D = 8, 64, 16, 512, 128
+    q, k, v = normal(31, (B, H, S, D)), normal(32, (B, Hk, S, D)), normal(33, (B, Hk, S, D))
+    tq, tk, tv = (to_torch(a, torch.bfloat16, cuda) for a in (q, k, v))
+    rope = build_rope_cache(S, D, theta=500000.0, device=cuda)
+    # a (B, S, H, D) output layout, as an engine keeps it, viewed as (B, H, S, D)
+    out = torch.full((B, S, H, D), float("nan"), dtype=torch.bfloat16, device=cuda)
+    copies = [torch.full_like(out, float("nan")) for _ in range(n_copies)]
+    view = out.transpose(1, 2)
+    res = flash_attention(tq, tk, tv, True, rope=rope, out=view,
+                          out_peers=[c.data_ptr() for c in copies])
+    torch.cuda.synchronize()
+    assert res.data_ptr() == view.data_ptr()
+    assert _lib.device_status(clear=True) == 0
+    for i, c in enumerate(copies):
+        assert torch.equal(c, out), f"copy {i} differs from the local output"
+    c_, s_ = oracle.build_rope_cache(S, D, 500000.0)
+    assert_close_attn(to_np(view), oracle.prefill_case_ref(q, k, v, c_, s_, causal=True),
+                      what="local output")
