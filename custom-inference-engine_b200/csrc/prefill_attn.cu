@@ -77,11 +77,6 @@ constexpr int kRegsSoftmax = D >= 128 ? 208 : 216;
 #define CIE_MAX_CHAINS 8
 #endif
 constexpr int kMaxPeers = 7;     // other GPUs an output tile can be copied to
-// Peers the softmax warpgroups write straight from registers in their epilogue;
-// the copy warp serves the rest from the stored rows.
-#ifndef CIE_PEER_DIRECT
-#define CIE_PEER_DIRECT 0
-#endif
 constexpr int kBM = 128;         // rows of one query tile; a CTA owns two
 constexpr int kBN = 128;         // keys per K/V tile
 
@@ -371,7 +366,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 v[i] = *reinterpret_cast<const vec_t*>(src + off[i]);
               }
             }
-            for (int pe = min(CIE_PEER_DIRECT, p.n_peers); pe < p.n_peers; ++pe) {
+            for (int pe = 0; pe < p.n_peers; ++pe) {
               uint8_t* dst = reinterpret_cast<uint8_t*>(p.o_peers[pe]);
 #pragma unroll
               for (int i = 0; i < kVec; ++i)
@@ -857,18 +852,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e)
               dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
-            if (CIE_PEER_DIRECT > 0) {
-              const int64_t off = reinterpret_cast<const uint8_t*>(o + c * 32) -
-                                  reinterpret_cast<const uint8_t*>(p.o);
-              const int nd = min(CIE_PEER_DIRECT, p.n_peers);
-              for (int pe = 0; pe < nd; ++pe) {
-                uint4* pdst = reinterpret_cast<uint4*>(
-                    reinterpret_cast<uint8_t*>(p.o_peers[pe]) + off);
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  pdst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
-              }
-            }
           }
         }
         tc_fence_before();
