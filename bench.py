@@ -109,7 +109,10 @@ def prefill_flops(B, Hq, S, d, M=None, N=None):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    """SM clock and clock-event reasons of this process's GPU, sampled through NVML
+    every 5 ms by a background thread while the timed region runs (a timed region
+    of tens of ms gets several samples). Falls back to nvidia-smi at 200 ms when
+    NVML is unavailable. Reads only; changes no setting."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -118,8 +121,46 @@ class ClockSampler:
     def __init__(self):
         self.proc = None
         self.path = None
+        self.thread = None
+        self.samples = []
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        prop = torch.cuda.get_device_properties(torch.cuda.current_device())
+        bus = f"{prop.pci_domain_id:08X}:{prop.pci_bus_id:02X}:{prop.pci_device_id:02X}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
 
     def start(self):
+        import threading
+
+        try:
+            nv, h = self._nvml_handle()
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - fall back to the nvidia-smi sampler
+            return self._start_smi()
+        self.stop_evt = threading.Event()
+        names = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                 "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                 "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+
+        def run():
+            while not self.stop_evt.is_set():
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((mhz, [n for n, b in names.items() if bits & b]))
+                except Exception:  # noqa: BLE001
+                    pass
+                self.stop_evt.wait(0.005)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+
+    def _start_smi(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
@@ -130,6 +171,19 @@ class ClockSampler:
             self.proc = None
 
     def stop(self) -> dict:
+        if self.thread is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=2)
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                        "source": "nvml"}
+            reasons = sorted({r for _, rs in self.samples for r in rs})
+            return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                    "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml, every 5 ms"}
+        return self._stop_smi()
+
+    def _stop_smi(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -149,13 +203,6 @@ class ClockSampler:
             except ValueError:
                 continue
         os.unlink(self.path)
-        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-        if vis:
-            try:
-                keep = {int(x) for x in vis.split(",")}
-                rows = [r for r in rows if r["idx"] in keep] or rows
-            except ValueError:
-                pass
         loaded = [r for r in rows if r["util"] > 0] or rows
         if not loaded:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
@@ -167,7 +214,7 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
                 "sm_max_mhz": max(r["smax"] for r in loaded), "reasons": sorted(reasons),
-                "samples": len(loaded)}
+                "samples": len(loaded), "source": "nvidia-smi, every 200 ms"}
 
 
 # ---------------------------------------------------------------- distributed
@@ -585,6 +632,27 @@ def e2e_prefill(cfg, world, rank, steps, warmup):
     return prefill_flops(B, cfg["Hq"], S, d) / (ms * 1e-3) / 1e12, h2d, d2h
 
 
+def time_all_gather(nbytes_per_rank, world, reps=10):
+    """ms of one NCCL all_gather_into_tensor of nbytes_per_rank from every rank
+    (CUDA events, max over ranks), with nothing else running."""
+    import torch
+    import torch.distributed as dist
+
+    src = torch.empty(nbytes_per_rank, dtype=torch.uint8, device="cuda")
+    dst = torch.empty(nbytes_per_rank * world, dtype=torch.uint8, device="cuda")
+    dist.all_gather_into_tensor(dst, src)
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        dist.all_gather_into_tensor(dst, src)
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e) / reps, world)
+    del src, dst
+    return ms
+
+
 def measure_pcie(world, mib=256, reps=5):
     """Pinned host<->device copy bandwidth of this rank while every rank copies at
     the same time (the condition the e2e leg runs in): GB/s H2D and D2H, max time
@@ -945,6 +1013,16 @@ def main():
     launches = args.steps * ((3 if wl.peer is not None else 1 + wl.chunks) if world > 1 else 2)
     gather_mode = wl.gather
     check = wl.check_against_one_gpu() if world > 1 else None
+    # scaling, split: the attention launches alone (with their in-kernel peer copies
+    # on the fused path) and, at N > 1, an NCCL all-gather of this rank's output
+    # timed alone (the collective the fused path replaces)
+    split = {"kernel_only_value": wl.flops_total / (kern_ms * 1e-3) / 1e12,
+             "kernel_ms": kern_ms, "step_ms": ms_step}
+    if world > 1:
+        split["nccl_all_gather_alone_ms"] = time_all_gather(wl.q.numel() * 2, world)
+        split["note"] = ("kernel_only_value: whole-job TFLOP/s if a step were only the "
+                         "attention launches (max over ranks); on the fused path they include "
+                         "the NVLink copies of the output")
     del wl
     torch.cuda.empty_cache()
 
@@ -1043,6 +1121,7 @@ def main():
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": launches, "device_status": status, "workloads": workloads,
         }
+        line["scaling_split"] = split
         if check is not None:
             line["multi_gpu_check"] = check
         print(json.dumps(line), flush=True)

@@ -102,11 +102,6 @@ class PeerOutput:
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
         self.device = torch.device(device)
-        if hasattr(symm_mem, "enable_symm_mem_for_group"):
-            try:
-                symm_mem.enable_symm_mem_for_group(self.group.group_name)
-            except Exception:  # newer releases enable groups on first use
-                pass
         self.bufs, self.hdls = [], []
         for _ in range(2):
             t = symm_mem.empty(*shape, dtype=dtype, device=self.device)
