@@ -334,3 +334,65 @@ def to_t(x, device):
     import torch
 
     return torch.from_numpy(np.ascontiguousarray(x)).to(device=device, dtype=torch.bfloat16)
+
+
+def test_verify_loop_has_no_host_sync(cuda):
+    """A speculative decoding round on the batched path — reserve and pack the
+    tables for a verify block (begin_step), fused append + paged attention for every
+    layer, roll the rejected drafts back, fork a sequence, then a decode step —
+    runs with torch's sync debug mode set to raise on any host synchronisation:
+    block tables reach the device through pinned non-blocking copies, the kernels
+    are asynchronous, and rollback is host bookkeeping. The same device work of a
+    step is then captured in a CUDA graph and replayed with the same result."""
+    import torch
+
+    from engine.attention import attention_forward_batch, begin_step
+    from kernels import build_rope_cache
+
+    hq, hkv, d, B, layers = 8, 2, 128, 3, 2
+    rope = build_rope_cache(4096, d, theta=500000.0, device=cuda)
+    cache = _cache(layers, hkv, d, cuda, blocks=256, bs=16)
+    tables = [cache.new_sequence() for _ in range(B)]
+    g = torch.Generator().manual_seed(11)
+
+    def rnd(*s):
+        return torch.randn(*s, generator=g).to(cuda, torch.bfloat16)
+
+    prompt = [rnd(B, h, 300, d) for h in (hq, hkv, hkv)]
+    verify = [rnd(B, h, 5, d) for h in (hq, hkv, hkv)]
+    dec = [rnd(B, h, 1, d) for h in (hq, hkv, hkv)]
+    step = begin_step(cache, tables, 300)
+    for layer in range(layers):
+        attention_forward_batch(*prompt, cache, layer, step, rope=rope)
+    torch.cuda.synchronize()
+
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        step = begin_step(cache, tables, 5)                     # verify block, M = gamma + 1
+        outs = [attention_forward_batch(*verify, cache, layer, step, rope=rope)
+                for layer in range(layers)]
+        for t, accepted in zip(tables, (0, 2, 4)):              # rejected drafts roll back
+            cache.rollback(t, t.length - (4 - accepted))
+        forked = cache.fork(tables[1])
+        step = begin_step(cache, tables, 1)                     # next decode step
+        for layer in range(layers):
+            attention_forward_batch(*dec, cache, layer, step, rope=rope)
+    finally:
+        torch.cuda.set_sync_debug_mode(0)
+    torch.cuda.synchronize()
+    assert forked.length == tables[1].length - 1
+    assert all(torch.isfinite(o.float()).all() for o in outs)
+
+    # the device work of one decode step as a CUDA graph
+    step = begin_step(cache, tables, 1)
+    eager = [attention_forward_batch(*dec, cache, layer, step, rope=rope)
+             for layer in range(layers)]
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured = [attention_forward_batch(*dec, cache, layer, step, rope=rope)
+                    for layer in range(layers)]
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(eager, captured):
+        assert torch.equal(a, b)
