@@ -608,74 +608,85 @@ __global__ void __launch_bounds__(kPagedWarps * 32)
 }
 
 // Log-sum-exp merge of split-KV partitions (sequences with >1 split only).
-// One CTA per (sequence, kv head, row group): row weights are computed once
-// into shared memory, then every thread combines float4 slices of the rows.
+// One CTA per (sequence, kv head, row group) and slice of kMergeRows<D> rows,
+// one thread per float4 column of a row: the CTA stages its rows' partition
+// log-sum-exps in shared memory with all threads at once, then every thread
+// walks the partitions with its loads unrolled, so the merge costs a few L2
+// round trips however many partitions there are (a per-row serial walk over
+// the log-sum-exps cost ~15 us at 17 partitions). CTAs whose rows are all
+// padding (row >= G*M) return at once. Partitions past kMergeCap read their
+// log-sum-exp from global memory.
 constexpr int kMergeCap = 32;
+constexpr int kMergeThreads = 128;
+
+template <int D, int RG>
+__host__ __device__ constexpr int merge_rows() {
+  return (kMergeThreads / (D / 4)) < RG ? kMergeThreads / (D / 4) : RG;
+}
 
 template <int D, int RG, bool BF16, bool PAGED>
-__global__ void __launch_bounds__(256) paged_merge_kernel(const PagedParams p) {
-  __shared__ float s_w[RG][kMergeCap];
-  __shared__ float s_mx[RG];
-  __shared__ float s_inv[RG];
+__global__ void __launch_bounds__(kMergeThreads) paged_merge_kernel(const PagedParams p) {
+  constexpr int D4 = D / 4;
+  constexpr int RPC = merge_rows<D, RG>();
+  __shared__ float s_lse[RPC][kMergeCap];
   const int unit = blockIdx.x;
+  const int r0 = blockIdx.y * RPC;  // first row (within the row group) of this CTA
   const int rg = unit % p.row_groups;
   const int kvh = (unit / p.row_groups) % p.Hkv;
   const int b = unit / (p.row_groups * p.Hkv);
+  const int R = p.G * p.M;
+  if (rg * RG + r0 >= R) return;
   int kv_len = PAGED ? p.kv_lens[b] : p.dense_n;
   if (kv_len < 0) kv_len = 0;
   if (PAGED && kv_len > p.max_blocks * p.block_size) kv_len = p.max_blocks * p.block_size;
   const int nsplit = kv_len > 0 ? (kv_len + p.split_tokens - 1) / p.split_tokens : 1;
   if (nsplit <= 1) return;
-  const int R = p.G * p.M;
   const int64_t base = static_cast<int64_t>(unit) * p.max_splits * RG;
-  for (int r = threadIdx.x; r < RG; r += blockDim.x) {
-    float mx = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, p.part_lse[base + s * RG + r]);
-    float sum = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float w = mx == -INFINITY ? 0.f : ex2(p.part_lse[base + s * RG + r] - mx);
-      if (s < kMergeCap) s_w[r][s] = w;
-      sum += w;
-    }
-    s_mx[r] = mx;
-    s_inv[r] = sum > 0.f ? 1.0f / sum : __int_as_float(0x7fc00000);
+  const int ns_c = nsplit < kMergeCap ? nsplit : kMergeCap;
+  for (int i = threadIdx.x; i < RPC * ns_c; i += kMergeThreads) {
+    const int r = i / ns_c, s = i % ns_c;
+    s_lse[r][s] = __ldg(p.part_lse + base + s * RG + r0 + r);
   }
   __syncthreads();
+  const int lr = threadIdx.x / D4, c = threadIdx.x % D4;
+  const int r = r0 + lr;
+  if (lr >= RPC || r >= RG || rg * RG + r >= R) return;
+  const float* lse_g = p.part_lse + base + r;  // partition s at lse_g[s * RG]
+  float mx = -INFINITY;
+  for (int s = 0; s < ns_c; ++s) mx = fmaxf(mx, s_lse[lr][s]);
+  for (int s = ns_c; s < nsplit; ++s) mx = fmaxf(mx, __ldg(lse_g + s * RG));
+  // weights, their sum and the weighted rows in partition order
+  float sum = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* po = p.part_o + (base + r) * D + c * 4;  // partition s at po[s * RG * D]
+  auto add = [&](float lse, int s) {
+    const float w = mx == -INFINITY ? 0.f : ex2(lse - mx);
+    sum += w;
+    const float4 v = __ldg(reinterpret_cast<const float4*>(po + static_cast<int64_t>(s) * RG * D));
+    acc.x += w * v.x;
+    acc.y += w * v.y;
+    acc.z += w * v.z;
+    acc.w += w * v.w;
+  };
+#pragma unroll 8
+  for (int s = 0; s < ns_c; ++s) add(s_lse[lr][s], s);
+  for (int s = ns_c; s < nsplit; ++s) add(__ldg(lse_g + s * RG), s);
+  const float inv = sum > 0.f ? 1.0f / sum : __int_as_float(0x7fc00000);
+  const int gr = rg * RG + r;
+  const int gh = gr / p.M, m = gr % p.M;
+  const int h = kvh * p.G + gh;
   using elem_t = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  elem_t* o = reinterpret_cast<elem_t*>(p.o);
-  constexpr int D4 = D / 4;
-  for (int idx = threadIdx.x; idx < RG * D4; idx += blockDim.x) {
-    const int r = idx / D4, c = idx % D4;
-    const int gr = rg * RG + r;
-    if (gr >= R) continue;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < nsplit; ++s) {
-      const float w = s < kMergeCap ? s_w[r][s]
-                                    : (s_mx[r] == -INFINITY
-                                           ? 0.f
-                                           : ex2(p.part_lse[base + s * RG + r] - s_mx[r]));
-      const float4 v =
-          *reinterpret_cast<const float4*>(p.part_o + (base + s * RG + r) * D + c * 4);
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
-    }
-    const float inv = s_inv[r];
-    const int gh = gr / p.M, m = gr % p.M;
-    const int h = kvh * p.G + gh;
-    elem_t* dst = o + b * p.o_sb + h * p.o_sh + m * p.o_sm + c * 4;
-    if constexpr (BF16) {
-      dst[0] = __float2bfloat16_rn(acc.x * inv);
-      dst[1] = __float2bfloat16_rn(acc.y * inv);
-      dst[2] = __float2bfloat16_rn(acc.z * inv);
-      dst[3] = __float2bfloat16_rn(acc.w * inv);
-    } else {
-      dst[0] = __float2half_rn(acc.x * inv);
-      dst[1] = __float2half_rn(acc.y * inv);
-      dst[2] = __float2half_rn(acc.z * inv);
-      dst[3] = __float2half_rn(acc.w * inv);
-    }
+  elem_t* dst = reinterpret_cast<elem_t*>(p.o) + b * p.o_sb + h * p.o_sh + m * p.o_sm + c * 4;
+  if constexpr (BF16) {
+    dst[0] = __float2bfloat16_rn(acc.x * inv);
+    dst[1] = __float2bfloat16_rn(acc.y * inv);
+    dst[2] = __float2bfloat16_rn(acc.z * inv);
+    dst[3] = __float2bfloat16_rn(acc.w * inv);
+  } else {
+    dst[0] = __float2half_rn(acc.x * inv);
+    dst[1] = __float2half_rn(acc.y * inv);
+    dst[2] = __float2half_rn(acc.z * inv);
+    dst[3] = __float2half_rn(acc.w * inv);
   }
 }
 
@@ -759,8 +770,10 @@ static int launch_mma_t(const CUtensorMap& mk, const CUtensorMap& mv, const Page
   kern<<<grid, kPagedWarps * 32, smem, st>>>(mk, mv, prm);
   CIE_CHECK_LAUNCH("paged_attn_kernel");
   if (prm.max_splits > 1) {
-    paged_merge_kernel<D, 16 * MT, BF16, PAGED>
-        <<<prm.B * prm.Hkv * prm.row_groups, 256, 0, st>>>(prm);
+    constexpr int RG = 16 * MT;
+    const dim3 mgrid(prm.B * prm.Hkv * prm.row_groups,
+                     (RG + merge_rows<D, RG>() - 1) / merge_rows<D, RG>());
+    paged_merge_kernel<D, RG, BF16, PAGED><<<mgrid, kMergeThreads, 0, st>>>(prm);
     CIE_CHECK_LAUNCH("paged_merge_kernel");
   }
   return CIE_OK;
