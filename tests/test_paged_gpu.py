@@ -95,6 +95,8 @@ PAGED_CASES = [
     (2, 16, 2, 5, 64, 32, [900, 37]),           # G*M = 40 rows -> 4 m-tiles
     (2, 8, 1, 9, 128, 16, [400, 1000]),          # G*M = 72 rows -> 3 row groups
     (3, 2, 2, 1, 16, 4, [3, 50, 9]),            # reference tiny-model geometry
+    (2, 4, 2, 3, 16, 8, [200, 70]),             # d=16 over several partitions
+    (1, 8, 1, 5, 16, 16, [300]),                # d=16, G*M = 40 rows: 64-row groups
     (2, 4, 2, 3, 32, 16, [100, 3]),
     (2, 4, 2, 1, 256, 16, [100, 500]),
 ]
